@@ -1,0 +1,64 @@
+// Python bindings of the sm_100a extension (module agent_factory_3_b200._C).
+#include <torch/extension.h>
+
+#include "common.h"
+
+namespace af3 {
+void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor out,
+          int64_t epi, int64_t sched, int64_t M, int64_t N, int64_t K,
+          c10::optional<torch::Tensor> group_offsets, int64_t num_groups,
+          c10::optional<torch::Tensor> bias, int64_t bias_group_stride,
+          c10::optional<torch::Tensor> row_scale, c10::optional<torch::Tensor> aux,
+          c10::optional<torch::Tensor> out2, double alpha, double beta, double act_alpha,
+          double act_limit, c10::optional<torch::Tensor> labels, int64_t vocab_offset,
+          c10::optional<torch::Tensor> lse_part, c10::optional<torch::Tensor> label_logit,
+          c10::optional<torch::Tensor> row_stats, int64_t n_tiles_total, int64_t bn,
+          int64_t band, int64_t out_group_stride, int64_t max_ctas);
+void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
+void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor gates, bool replay);
+void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor offsets,
+               torch::Tensor expert_counts, torch::Tensor dest, torch::Tensor row_src,
+               torch::Tensor row_gate, torch::Tensor scratch);
+void gather_rows(torch::Tensor x, torch::Tensor src, c10::optional<torch::Tensor> scale,
+                 torch::Tensor out);
+void combine_rows(torch::Tensor y, torch::Tensor dest, int64_t K,
+                  c10::optional<torch::Tensor> residual, torch::Tensor out);
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y,
+                 c10::optional<torch::Tensor> rstd, double eps);
+void rmsnorm_bwd(torch::Tensor x, torch::Tensor w, torch::Tensor dy, torch::Tensor rstd,
+                 c10::optional<torch::Tensor> dres, torch::Tensor dx,
+                 c10::optional<torch::Tensor> dw);
+void rope_apply(torch::Tensor qkv, int64_t n_rot_heads, int64_t head_dim, torch::Tensor pos,
+                torch::Tensor cos_t, torch::Tensor sin_t, bool inverse);
+void lse_merge(torch::Tensor parts, torch::Tensor label_logit, torch::Tensor logprob,
+               torch::Tensor entropy, torch::Tensor logz);
+void swiglu_fwd(torch::Tensor gu, torch::Tensor out, double alpha, double limit);
+void swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu, double alpha,
+                double limit);
+}  // namespace af3
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  namespace py = pybind11;
+  m.doc() = "agent_factory_3_b200 sm_100a kernels";
+  m.def("gemm", &af3::gemm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
+        py::arg("out"), py::arg("epi"), py::arg("sched"), py::arg("M"), py::arg("N"),
+        py::arg("K"), py::arg("group_offsets"), py::arg("num_groups"), py::arg("bias"),
+        py::arg("bias_group_stride"), py::arg("row_scale"), py::arg("aux"), py::arg("out2"),
+        py::arg("alpha"), py::arg("beta"), py::arg("act_alpha"), py::arg("act_limit"),
+        py::arg("labels"), py::arg("vocab_offset"), py::arg("lse_part"),
+        py::arg("label_logit"), py::arg("row_stats"), py::arg("n_tiles_total"), py::arg("bn"),
+        py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"));
+  m.def("mxfp4_dequant", &af3::mxfp4_dequant);
+  m.def("moe_route", &af3::moe_route);
+  m.def("moe_group", &af3::moe_group);
+  m.def("gather_rows", &af3::gather_rows);
+  m.def("combine_rows", &af3::combine_rows);
+  m.def("rmsnorm_fwd", &af3::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &af3::rmsnorm_bwd);
+  m.def("rope_apply", &af3::rope_apply);
+  m.def("lse_merge", &af3::lse_merge);
+  m.def("swiglu_fwd", &af3::swiglu_fwd);
+  m.def("swiglu_bwd", &af3::swiglu_bwd);
+  m.def("device_error", &af3::device_error_take,
+        "Read and clear the current device's kernel error word (0 = no error).");
+}

@@ -1,0 +1,75 @@
+// Host-side launch of the tcgen05 GEMM: builds the TMA descriptors for the operand layouts
+// and launches the persistent kernel with one CTA per SM.
+#pragma once
+#include "gemm_sm100.cuh"
+#include "host_utils.h"
+
+namespace af3 {
+
+struct GemmOperands {
+  const void* a;
+  bool a_mn;
+  int64_t lda;  // elements between consecutive rows of the stored matrix
+  int64_t a_rows, a_cols;  // stored shape (rows x cols, row-major)
+  const void* b;
+  bool b_mn;
+  bool b_3d;
+  int64_t ldb;
+  int64_t b_rows, b_cols;  // per group (3-D: group g starts at b + g*b_gstride)
+  int64_t b_groups;
+  int64_t b_gstride;       // elements
+};
+
+template <int BN>
+inline void build_tmaps(const GemmOperands& o, CUtensorMap& ta, CUtensorMap& tb) {
+  const auto bf16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  {
+    uint64_t dims[2] = {(uint64_t)o.a_cols, (uint64_t)o.a_rows};
+    uint64_t strides[1] = {(uint64_t)o.lda * 2};
+    uint32_t box[2];
+    if (!o.a_mn) { box[0] = kBK; box[1] = kBM; }   // [M, K]: K inner
+    else { box[0] = 64; box[1] = kBK; }            // [K, M]: M inner, 64-wide chunks
+    ta = make_tmap(o.a, bf16, 2, dims, strides, box, sw);
+  }
+  {
+    uint32_t box[3];
+    if (!o.b_mn) { box[0] = kBK; box[1] = BN; box[2] = 1; }
+    else { box[0] = 64; box[1] = kBK; box[2] = 1; }
+    if (o.b_3d) {
+      uint64_t dims[3] = {(uint64_t)o.b_cols, (uint64_t)o.b_rows, (uint64_t)o.b_groups};
+      uint64_t strides[2] = {(uint64_t)o.ldb * 2, (uint64_t)o.b_gstride * 2};
+      tb = make_tmap(o.b, bf16, 3, dims, strides, box, sw);
+    } else {
+      uint64_t dims[2] = {(uint64_t)o.b_cols, (uint64_t)o.b_rows};
+      uint64_t strides[1] = {(uint64_t)o.ldb * 2};
+      tb = make_tmap(o.b, bf16, 2, dims, strides, box, sw);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI>
+inline void launch_gemm(const GemmOperands& o, const GemmArgs& args, int max_ctas,
+                        cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  build_tmaps<BN>(o, ta, tb);
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, B_3D, SCHED, EPI>;
+  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+  static bool attr_set = false;
+  if (!attr_set) {
+    AF3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  int ctas;
+  if (SCHED == kSchedPlain) {
+    const int64_t tiles = ((args.M + kBM - 1) / kBM) * (int64_t)((args.N + BN - 1) / BN);
+    ctas = (int)std::min<int64_t>(tiles, max_ctas);
+  } else {
+    ctas = max_ctas;  // tile count lives on the device
+  }
+  if (ctas <= 0) return;
+  kern<<<ctas, kGemmThreads, smem, stream>>>(ta, tb, args);
+  AF3_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace af3

@@ -1,0 +1,61 @@
+"""Loader of the in-tree sm_100a extension (``agent_factory_3_b200/_C*.so``).
+
+On a machine with a CUDA device the extension is mandatory: operators called with CUDA
+tensors raise instead of silently falling back to PyTorch.  On CPU-only machines the
+operators use their PyTorch reference implementations.
+"""
+from __future__ import annotations
+
+import importlib
+import os
+
+import torch
+
+_EXT = None
+_ERR: Exception | None = None
+
+
+def ext():
+    """Return the compiled extension module, importing it on first use."""
+    global _EXT, _ERR
+    if _EXT is not None:
+        return _EXT
+    if _ERR is not None:
+        raise RuntimeError(
+            "agent_factory_3_b200._C is not available; build it with "
+            "`python setup.py build_ext --inplace`"
+        ) from _ERR
+    try:
+        _EXT = importlib.import_module("agent_factory_3_b200._C")
+    except Exception as e:  # pragma: no cover - exercised on machines without the build
+        _ERR = e
+        raise RuntimeError(
+            "agent_factory_3_b200._C is not available; build it with "
+            "`python setup.py build_ext --inplace`"
+        ) from e
+    return _EXT
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def use_cuda_kernels(*tensors: torch.Tensor) -> bool:
+    """True when every tensor is on a CUDA device (the extension must then be present)."""
+    if not tensors or not all(t.is_cuda for t in tensors if t is not None):
+        return False
+    if os.environ.get("AF3_FORCE_TORCH_REFERENCE") == "1":
+        return False
+    ext()  # raise loudly if missing
+    return True
+
+
+def check_device_error() -> None:
+    """Raise if a bounded wait inside one of our kernels expired since the last check."""
+    code = ext().device_error()
+    if code != 0:
+        raise RuntimeError(f"agent_factory_3_b200 kernel reported error code {code}")
