@@ -13,7 +13,8 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           double act_limit, c10::optional<torch::Tensor> labels, int64_t vocab_offset,
           c10::optional<torch::Tensor> lse_part, c10::optional<torch::Tensor> label_logit,
           c10::optional<torch::Tensor> row_stats, int64_t n_tiles_total, int64_t bn,
-          int64_t band, int64_t out_group_stride, int64_t max_ctas);
+          int64_t band, int64_t out_group_stride, int64_t max_ctas,
+          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2);
 void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
 void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor gates, bool replay);
 void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor offsets,
@@ -47,7 +48,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha"), py::arg("beta"), py::arg("act_alpha"), py::arg("act_limit"),
         py::arg("labels"), py::arg("vocab_offset"), py::arg("lse_part"),
         py::arg("label_logit"), py::arg("row_stats"), py::arg("n_tiles_total"), py::arg("bn"),
-        py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"));
+        py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"),
+        py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("K2") = 0);
   m.def("mxfp4_dequant", &af3::mxfp4_dequant);
   m.def("moe_route", &af3::moe_route);
   m.def("moe_group", &af3::moe_group);

@@ -203,16 +203,26 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, int n_r
 void rope_apply(torch::Tensor qkv, int64_t n_rot_heads, int64_t head_dim, torch::Tensor pos,
                 torch::Tensor cos_t, torch::Tensor sin_t, bool inverse) {
   check_cuda_bf16(qkv, "qkv");
-  AF3_CHECK(head_dim == 64, "rope kernel instantiated for head_dim 64");
+  AF3_CHECK(head_dim == 16 || head_dim == 32 || head_dim == 64 || head_dim == 128,
+            "rope: head_dim must be 16, 32, 64 or 128");
   const int64_t T = qkv.size(0);
   const c10::cuda::CUDAGuard guard(qkv.device());
   if (T == 0) return;
   const int64_t total = T * n_rot_heads * (head_dim / 16);
   const int threads = 256;
-  rope_kernel<64><<<(total + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), (int)n_rot_heads,
-      pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T,
-      inverse ? -1.f : 1.f);
+  const int64_t grid = (total + threads - 1) / threads;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto* p = reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr());
+  const float sign = inverse ? -1.f : 1.f;
+#define AF3_ROPE(D)                                                                          \
+  rope_kernel<D><<<grid, threads, 0, stream>>>(p, qkv.stride(0), (int)n_rot_heads,           \
+                                              pos.data_ptr<int>(), cos_t.data_ptr<float>(),   \
+                                              sin_t.data_ptr<float>(), T, sign)
+  if (head_dim == 16) AF3_ROPE(16);
+  else if (head_dim == 32) AF3_ROPE(32);
+  else if (head_dim == 64) AF3_ROPE(64);
+  else AF3_ROPE(128);
+#undef AF3_ROPE
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -5,10 +5,6 @@
 
 namespace af3 {
 
-static const void* opt_ptr(const c10::optional<torch::Tensor>& t) {
-  return t.has_value() ? t->data_ptr() : nullptr;
-}
-
 void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor out,
           int64_t epi, int64_t sched, int64_t M, int64_t N, int64_t K,
           c10::optional<torch::Tensor> group_offsets, int64_t num_groups,
@@ -18,7 +14,8 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           double act_limit, c10::optional<torch::Tensor> labels, int64_t vocab_offset,
           c10::optional<torch::Tensor> lse_part, c10::optional<torch::Tensor> label_logit,
           c10::optional<torch::Tensor> row_stats, int64_t n_tiles_total, int64_t bn,
-          int64_t band, int64_t out_group_stride, int64_t max_ctas) {
+          int64_t band, int64_t out_group_stride, int64_t max_ctas,
+          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2) {
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
   AF3_CHECK(a.dim() == 2 && a.stride(1) == 1, "a must be 2-D with unit inner stride");
@@ -42,7 +39,24 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
   o.b_groups = o.b_3d ? b.size(0) : 1;
   o.b_gstride = o.b_3d ? b.stride(0) : 0;
 
+  const bool dual = a2.has_value() && b2.has_value() && K2 > 0;
+  if (dual) {
+    check_cuda_bf16(*a2, "a2");
+    check_cuda_bf16(*b2, "b2");
+    AF3_CHECK(a2->dim() == 2 && a2->stride(1) == 1, "a2 must be 2-D, unit inner stride");
+    AF3_CHECK(b2->dim() == b.dim() && b2->stride(-1) == 1, "b2 must match b's rank");
+    o.a2 = a2->data_ptr();
+    o.lda2 = a2->stride(0);
+    o.a2_rows = a2->size(0);
+    o.a2_cols = a2->size(1);
+    o.b2 = b2->data_ptr();
+    o.ldb2 = b2->stride(-2);
+    o.b2_rows = b2->size(-2);
+    o.b2_cols = b2->size(-1);
+    o.b2_gstride = b2->dim() == 3 ? b2->stride(0) : 0;
+  }
   GemmArgs args{};
+  args.K2 = dual ? (int)K2 : 0;
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
@@ -78,16 +92,19 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
   }
   int ctas = max_ctas > 0 ? (int)max_ctas : num_sms();
   auto stream = at::cuda::getCurrentCUDAStream().stream();
-  bool ok;
-  if (sched == kSchedPlain)
-    ok = gemm_dispatch_plain((int)bn, a_mn, b_mn, (int)epi, o, args, ctas, stream);
-  else
-    ok = gemm_dispatch_grouped((int)bn, a_mn, b_mn, o.b_3d, (int)sched, (int)epi, o, args,
-                               ctas, stream);
+  const GemmKey key{(int)bn, a_mn, b_mn, o.b_3d, (int)sched, (int)epi, dual};
+  bool ok = false;
+  if (sched == kSchedPlain) {
+    ok = b_mn ? gemm_dispatch_dense_bwd(key, o, args, ctas, stream)
+              : gemm_dispatch_dense_fwd(key, o, args, ctas, stream);
+  } else {
+    ok = (b_mn || sched == kSchedGroupedK) ? gemm_dispatch_grouped_bwd(key, o, args, ctas, stream)
+                                           : gemm_dispatch_grouped_fwd(key, o, args, ctas, stream);
+  }
   AF3_CHECK(ok, "no GEMM variant for bn=" + std::to_string(bn) + " a_mn=" +
                     std::to_string(a_mn) + " b_mn=" + std::to_string(b_mn) + " b_3d=" +
                     std::to_string(o.b_3d) + " sched=" + std::to_string(sched) +
-                    " epi=" + std::to_string(epi));
+                    " epi=" + std::to_string(epi) + " dual=" + std::to_string(dual));
 }
 
 }  // namespace af3

@@ -18,47 +18,63 @@ struct GemmOperands {
   int64_t b_rows, b_cols;  // per group (3-D: group g starts at b + g*b_gstride)
   int64_t b_groups;
   int64_t b_gstride;       // elements
+  // second operand pair (dual mode); same majors as (a, b)
+  const void* a2 = nullptr;
+  int64_t lda2 = 0, a2_rows = 0, a2_cols = 0;
+  const void* b2 = nullptr;
+  int64_t ldb2 = 0, b2_rows = 0, b2_cols = 0, b2_gstride = 0;
 };
 
 template <int BN>
-inline void build_tmaps(const GemmOperands& o, CUtensorMap& ta, CUtensorMap& tb) {
+inline void build_tmaps(const GemmOperands& o, CUtensorMap& ta, CUtensorMap& tb, bool second) {
   const auto bf16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  const void* pa = second ? o.a2 : o.a;
+  const int64_t lda = second ? o.lda2 : o.lda, a_rows = second ? o.a2_rows : o.a_rows,
+                a_cols = second ? o.a2_cols : o.a_cols;
+  const void* pb = second ? o.b2 : o.b;
+  const int64_t ldb = second ? o.ldb2 : o.ldb, b_rows = second ? o.b2_rows : o.b_rows,
+                b_cols = second ? o.b2_cols : o.b_cols,
+                b_gstride = second ? o.b2_gstride : o.b_gstride;
   {
-    uint64_t dims[2] = {(uint64_t)o.a_cols, (uint64_t)o.a_rows};
-    uint64_t strides[1] = {(uint64_t)o.lda * 2};
+    uint64_t dims[2] = {(uint64_t)a_cols, (uint64_t)a_rows};
+    uint64_t strides[1] = {(uint64_t)lda * 2};
     uint32_t box[2];
     if (!o.a_mn) { box[0] = kBK; box[1] = kBM; }   // [M, K]: K inner
     else { box[0] = 64; box[1] = kBK; }            // [K, M]: M inner, 64-wide chunks
-    ta = make_tmap(o.a, bf16, 2, dims, strides, box, sw);
+    ta = make_tmap(pa, bf16, 2, dims, strides, box, sw);
   }
   {
     uint32_t box[3];
     if (!o.b_mn) { box[0] = kBK; box[1] = BN; box[2] = 1; }
     else { box[0] = 64; box[1] = kBK; box[2] = 1; }
     if (o.b_3d) {
-      uint64_t dims[3] = {(uint64_t)o.b_cols, (uint64_t)o.b_rows, (uint64_t)o.b_groups};
-      uint64_t strides[2] = {(uint64_t)o.ldb * 2, (uint64_t)o.b_gstride * 2};
-      tb = make_tmap(o.b, bf16, 3, dims, strides, box, sw);
+      uint64_t dims[3] = {(uint64_t)b_cols, (uint64_t)b_rows, (uint64_t)o.b_groups};
+      uint64_t strides[2] = {(uint64_t)ldb * 2, (uint64_t)b_gstride * 2};
+      tb = make_tmap(pb, bf16, 3, dims, strides, box, sw);
     } else {
-      uint64_t dims[2] = {(uint64_t)o.b_cols, (uint64_t)o.b_rows};
-      uint64_t strides[1] = {(uint64_t)o.ldb * 2};
-      tb = make_tmap(o.b, bf16, 2, dims, strides, box, sw);
+      uint64_t dims[2] = {(uint64_t)b_cols, (uint64_t)b_rows};
+      uint64_t strides[1] = {(uint64_t)ldb * 2};
+      tb = make_tmap(pb, bf16, 2, dims, strides, box, sw);
     }
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI>
+template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI, bool DUAL = false>
 inline void launch_gemm(const GemmOperands& o, const GemmArgs& args, int max_ctas,
                         cudaStream_t stream) {
-  CUtensorMap ta, tb;
-  build_tmaps<BN>(o, ta, tb);
-  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, B_3D, SCHED, EPI>;
+  CUtensorMap ta, tb, ta2, tb2;
+  build_tmaps<BN>(o, ta, tb, false);
+  if (DUAL) build_tmaps<BN>(o, ta2, tb2, true);
+  else { ta2 = ta; tb2 = tb; }
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, B_3D, SCHED, EPI, DUAL>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per device
+  int dev = 0;
+  AF3_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev >= 64 || !attr_set[dev]) {
     AF3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
+    if (dev < 64) attr_set[dev] = true;
   }
   int ctas;
   if (SCHED == kSchedPlain) {
@@ -68,7 +84,7 @@ inline void launch_gemm(const GemmOperands& o, const GemmArgs& args, int max_cta
     ctas = max_ctas;  // tile count lives on the device
   }
   if (ctas <= 0) return;
-  kern<<<ctas, kGemmThreads, smem, stream>>>(ta, tb, args);
+  kern<<<ctas, kGemmThreads, smem, stream>>>(ta, tb, ta2, tb2, args);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

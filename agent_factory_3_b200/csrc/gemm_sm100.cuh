@@ -39,6 +39,7 @@ enum EpiKind : int {
 
 struct GemmArgs {
   int M, N, K;
+  int K2;                    // dual-operand mode: extra reduction over (A2, B2), 0 = off
   int num_groups;
   const int* group_offsets;  // [G+1] (grouped modes)
   int band;                  // raster band (M tiles) for L2 reuse
@@ -347,10 +348,15 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, int row, bool row_o
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI>
+// DUAL: after the main K loop, K2 more columns are reduced from a second operand pair
+// (A2, B2) with the same majors -- e.g. the LoRA branch [x | s*x*A^T] x [W | B]^T of a
+// LoRA-adapted linear layer runs as one GEMM.
+template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI, bool DUAL>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tma_a,
-                      const __grid_constant__ CUtensorMap tma_b, const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tma_b,
+                      const __grid_constant__ CUtensorMap tma_a2,
+                      const __grid_constant__ CUtensorMap tma_b2, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -403,6 +409,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (DUAL) {
+      tma_prefetch_desc(&tma_a2);
+      tma_prefetch_desc(&tma_b2);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
@@ -431,26 +441,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       TileCoord tc;
       for (int t = blockIdx.x; get_tile<SCHED>(t, args, BN, prefix, tc); t += gridDim.x) {
-        for (int k = tc.k_begin; k < tc.k_end; k += kBK) {
+        const int nk1 = (tc.k_end - tc.k_begin + kBK - 1) / kBK;
+        const int nk = nk1 + (DUAL ? (args.K2 + kBK - 1) / kBK : 0);
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
           uint8_t* sa = tiles + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
+          const bool second = DUAL && kb >= nk1;
+          const CUtensorMap* ma = second ? &tma_a2 : &tma_a;
+          const CUtensorMap* mb = second ? &tma_b2 : &tma_b;
+          const int k = second ? (kb - nk1) * kBK : tc.k_begin + kb * kBK;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           if (!A_MN) {
-            tma_load_2d(sa, &tma_a, &full_bar[stage], k, tc.m0);
+            tma_load_2d(sa, ma, &full_bar[stage], k, tc.m0);
           } else {
 #pragma unroll
             for (int c = 0; c < kBM / 64; ++c)
-              tma_load_2d(sa + c * 8192, &tma_a, &full_bar[stage], tc.m0 + c * 64, k);
+              tma_load_2d(sa + c * 8192, ma, &full_bar[stage], tc.m0 + c * 64, k);
           }
           if (!B_MN) {
-            if (B_3D) tma_load_3d(sb, &tma_b, &full_bar[stage], k, tc.n0, tc.g);
-            else tma_load_2d(sb, &tma_b, &full_bar[stage], k, tc.n0);
+            if (B_3D) tma_load_3d(sb, mb, &full_bar[stage], k, tc.n0, tc.g);
+            else tma_load_2d(sb, mb, &full_bar[stage], k, tc.n0);
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c) {
-              if (B_3D) tma_load_3d(sb + c * 8192, &tma_b, &full_bar[stage], tc.n0 + c * 64, k, tc.g);
-              else tma_load_2d(sb + c * 8192, &tma_b, &full_bar[stage], tc.n0 + c * 64, k);
+              if (B_3D) tma_load_3d(sb + c * 8192, mb, &full_bar[stage], tc.n0 + c * 64, k, tc.g);
+              else tma_load_2d(sb + c * 8192, mb, &full_bar[stage], tc.n0 + c * 64, k);
             }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -473,7 +489,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * BN;
         uint32_t accum = 0;
         bool ok = true;
-        for (int k = tc.k_begin; k < tc.k_end; k += kBK) {
+        const int nk = (tc.k_end - tc.k_begin + kBK - 1) / kBK +
+                       (DUAL ? (args.K2 + kBK - 1) / kBK : 0);
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, args.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(tiles + stage * Cfg::STAGE_BYTES);

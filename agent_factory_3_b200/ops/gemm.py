@@ -36,11 +36,11 @@ def _call(a, a_mn, b, b_mn, out, epi, sched, M, N, K, *, offsets=None, num_group
           bias_gstride=0, row_scale=None, aux=None, out2=None, alpha=1.0, beta=0.0,
           act_alpha=SWIGLU_ALPHA, act_limit=SWIGLU_LIMIT, labels=None, vocab_offset=0,
           lse_part=None, label_logit=None, row_stats=None, n_tiles_total=0, bn=256, band=8,
-          out_group_stride=0, max_ctas=0):
+          out_group_stride=0, max_ctas=0, a2=None, b2=None, K2=0):
     ext().gemm(a, a_mn, b, b_mn, out, epi, sched, M, N, K, offsets, num_groups, bias,
                bias_gstride, row_scale, aux, out2, float(alpha), float(beta), float(act_alpha),
                float(act_limit), labels, vocab_offset, lse_part, label_logit, row_stats,
-               n_tiles_total, bn, band, out_group_stride, max_ctas)
+               n_tiles_total, bn, band, out_group_stride, max_ctas, a2, b2, K2)
 
 
 def _as_mk(a: torch.Tensor, layout: str) -> torch.Tensor:
@@ -55,8 +55,11 @@ def _as_kn(b: torch.Tensor, layout: str) -> torch.Tensor:
 # dense
 # ------------------------------------------------------------------------------------
 def matmul_reference(a, b, a_layout="mk", b_layout="nk", bias=None, alpha=1.0, residual=None,
-                     out_dtype=torch.bfloat16, accumulate_into=None):
-    y = (_as_mk(a, a_layout).float() @ _as_kn(b, b_layout).float()) * alpha
+                     out_dtype=torch.bfloat16, accumulate_into=None, a2=None, b2=None):
+    y = _as_mk(a, a_layout).float() @ _as_kn(b, b_layout).float()
+    if a2 is not None:
+        y = y + _as_mk(a2, a_layout).float() @ _as_kn(b2, b_layout).float()
+    y = y * alpha
     if bias is not None:
         y = y + bias.float()
     if residual is not None:
@@ -68,13 +71,21 @@ def matmul_reference(a, b, a_layout="mk", b_layout="nk", bias=None, alpha=1.0, r
 
 def matmul(a: torch.Tensor, b: torch.Tensor, *, a_layout: str = "mk", b_layout: str = "nk",
            bias: torch.Tensor | None = None, alpha: float = 1.0,
-           residual: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+           residual: torch.Tensor | None = None, out_dtype=None,
            out: torch.Tensor | None = None, accumulate: bool = False, bn: int | None = None,
-           band: int = 8) -> torch.Tensor:
-    """C = alpha * A @ B (+ bias) (+ residual).  ``accumulate`` (fp32 out only): C += ...."""
+           band: int = 8, a2: torch.Tensor | None = None,
+           b2: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * (A @ B [+ A2 @ B2]) (+ bias) (+ residual).  ``accumulate`` (fp32 out):
+    C += ....  The optional second pair (same layouts) extends the reduction; it carries the
+    LoRA branch of an adapted linear layer.  ``out_dtype`` defaults to bf16 (fp32 inputs on
+    the reference path keep fp32)."""
+    if out_dtype is None:
+        out_dtype = out.dtype if out is not None else (
+            torch.float32 if a.dtype == torch.float32 else torch.bfloat16)
     if not use_cuda_kernels(a, b):
         acc = out if (accumulate and out is not None) else None
-        y = matmul_reference(a, b, a_layout, b_layout, bias, alpha, residual, out_dtype, acc)
+        y = matmul_reference(a, b, a_layout, b_layout, bias, alpha, residual, out_dtype, acc,
+                             a2, b2)
         if out is not None:
             out.copy_(y)
             return out
@@ -87,14 +98,28 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_layout: str = "mk", b_layout: 
     assert (b.shape[0] if b_mn else b.shape[1]) == K, "inner dimensions differ"
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    dual = a2 is not None
     if bn is None:
-        allowed = (256, 128, 64) if (b_mn or a_mn) else (256, 128, 64, 32)
+        if dual:
+            allowed = (256, 192) if b_mn else (256, 192, 128)
+        elif a_mn:
+            allowed = (256, 192, 128, 64)
+        elif b_mn:
+            allowed = (256, 192, 128, 64)
+        else:
+            allowed = (256, 192, 128, 64, 32)
         bn = pick_bn(N, allowed)
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     assert residual is None or epi == EPI_BF16
+    K2 = 0
+    if dual:
+        K2 = a2.shape[0] if a_mn else a2.shape[1]
+        a2 = a2 if a2.stride(-1) == 1 else a2.contiguous()
+        b2 = b2 if b2.stride(-1) == 1 else b2.contiguous()
     _call(a.contiguous() if a.stride(-1) != 1 else a, a_mn,
           b.contiguous() if b.stride(-1) != 1 else b, b_mn, out, epi, SCHED_PLAIN, M, N, K,
-          bias=bias, aux=residual, alpha=alpha, beta=1.0 if accumulate else 0.0, bn=bn, band=band)
+          bias=bias, aux=residual, alpha=alpha, beta=1.0 if accumulate else 0.0, bn=bn, band=band,
+          a2=a2, b2=b2, K2=K2)
     return out
 
 
@@ -116,7 +141,7 @@ def swiglu_reference(gate_up: torch.Tensor, alpha=SWIGLU_ALPHA, limit=SWIGLU_LIM
 
 def grouped_matmul_reference(a, b, offsets, b_layout="nk", epilogue="bf16", bias=None,
                              row_scale=None, aux=None, alpha=1.0, act_alpha=SWIGLU_ALPHA,
-                             act_limit=SWIGLU_LIMIT):
+                             act_limit=SWIGLU_LIMIT, a2=None, b2=None):
     """Reference of :func:`grouped_matmul`; returns (out, out2)."""
     R = a.shape[0]
     N = b.shape[1] if b_layout == "nk" else b.shape[2]
@@ -126,24 +151,28 @@ def grouped_matmul_reference(a, b, offsets, b_layout="nk", epilogue="bf16", bias
             continue
         w = b[g].float()
         y = a[s:e].float() @ (w.t() if b_layout == "nk" else w)
+        if a2 is not None:
+            w2 = b2[g].float()
+            y = y + a2[s:e].float() @ (w2.t() if b_layout == "nk" else w2)
         y = y * alpha
         if bias is not None:
             y = y + bias[g].float()
         res[s:e] = y
     out2 = None
+    od = torch.float32 if a.dtype == torch.float32 else torch.bfloat16
     if epilogue == "bf16":
-        out = res.to(torch.bfloat16)
+        out = res.to(od)
     elif epilogue == "rowscale":
-        out = (res * row_scale.float()[:R, None]).to(torch.bfloat16)
+        out = (res * row_scale.float()[:R, None]).to(od)
     elif epilogue == "swiglu":
-        out2 = res.to(torch.bfloat16)
-        out = swiglu_reference(out2.float(), act_alpha, act_limit).to(torch.bfloat16)
+        out2 = res.to(od)
+        out = swiglu_reference(out2.float(), act_alpha, act_limit).to(od)
     elif epilogue == "swiglu_bwd":
-        gu = aux.float()
-        gu.requires_grad_(True)
-        h = swiglu_reference(gu, act_alpha, act_limit)
-        (dgu,) = torch.autograd.grad(h, gu, res)
-        out = dgu.to(torch.bfloat16)
+        with torch.enable_grad():
+            gu = aux.detach().float().requires_grad_(True)
+            h = swiglu_reference(gu, act_alpha, act_limit)
+            (dgu,) = torch.autograd.grad(h, gu, res)
+        out = dgu.to(od)
     else:
         raise ValueError(epilogue)
     return out, out2
@@ -155,7 +184,8 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
                    aux: torch.Tensor | None = None, out: torch.Tensor | None = None,
                    out2: torch.Tensor | None = None, alpha: float = 1.0,
                    act_alpha: float = SWIGLU_ALPHA, act_limit: float = SWIGLU_LIMIT,
-                   save_preact: bool = False, bn: int | None = None, band: int = 4):
+                   save_preact: bool = False, bn: int | None = None, band: int = 4,
+                   a2: torch.Tensor | None = None, b2: torch.Tensor | None = None):
     """Per-expert GEMM over the expert-sorted, 128-row padded activation buffer.
 
     a: [R, K] sorted rows; b: [G, N, K] ("nk") or [G, K, N] ("kn"); offsets: int32 [G+1]
@@ -169,7 +199,7 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
     """
     if not use_cuda_kernels(a, b):
         o, o2 = grouped_matmul_reference(a, b, offsets, b_layout, epilogue, bias, row_scale, aux,
-                                         alpha, act_alpha, act_limit)
+                                         alpha, act_alpha, act_limit, a2, b2)
         if out is not None:
             out.copy_(o)
             o = out
@@ -186,17 +216,22 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
         out = torch.empty(R, cols, device=a.device, dtype=torch.bfloat16)
     if epi == EPI_SWIGLU and save_preact and out2 is None:
         out2 = torch.empty(R, N, device=a.device, dtype=torch.bfloat16)
+    dual = a2 is not None
     if bn is None:
-        allowed = (256, 192, 128) if N >= 128 else (128, 64, 32)
-        if b_mn:
-            allowed = tuple(x for x in allowed if x >= 64) or (64,)
+        if dual:
+            allowed = (256, 192)
+        elif N >= 128:
+            allowed = (256, 192, 128)
+        else:
+            allowed = (64,) if b_mn else (32,)
         bn = pick_bn(N, allowed)
     if epi in (EPI_SWIGLU,):
         assert N % 32 == 0
     _call(a, False, b, b_mn, out, epi, SCHED_GROUPED_M, R, N, K, offsets=offsets, num_groups=G,
           bias=bias, bias_gstride=(bias.stride(0) if bias is not None else 0),
           row_scale=row_scale, aux=aux, out2=out2 if epi == EPI_SWIGLU else None, alpha=alpha,
-          act_alpha=act_alpha, act_limit=act_limit, bn=bn, band=band)
+          act_alpha=act_alpha, act_limit=act_limit, bn=bn, band=band, a2=a2, b2=b2,
+          K2=(a2.shape[1] if dual else 0))
     return out, (out2 if epi == EPI_SWIGLU else None)
 
 

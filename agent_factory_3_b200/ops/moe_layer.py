@@ -1,0 +1,146 @@
+"""Routed MoE MLP of gpt-oss with frozen MXFP4 experts and optional per-expert LoRA.
+
+Forward (one token batch, T tokens, top-K):
+  logits = x Wr^T + br                         tcgen05 GEMM, fp32 out
+  ids, gates = top-K(logits) or replay ids     softmax over the K chosen logits
+  grouping -> 128-row padded expert segments   (deterministic, stable by token order)
+  x_s = gather(x)                              [R, H]
+  [xa]  = s * x_s A_gu_e^T                     LoRA down-projection, [R, r]
+  h, gu = SwiGLU([x_s | xa] [W_gu_e | B_gu_e]^T + b_gu_e)     one grouped GEMM, fused epilogue
+  [ha]  = s * h A_dn_e^T
+  y_s   = gate * ([h | ha] [W_dn_e | B_dn_e]^T + b_dn_e)       one grouped GEMM, fused gates
+  out   = residual + sum_k y_s[dest[t, k]]     combine
+
+Backward computes dx and the LoRA gradients only (experts and router are frozen).  As in the
+reference (models/gpt_oss/quantization.py:376-421), no gradient flows into the gate weights
+or router logits, and the expert weights are re-derived from the MXFP4 bytes instead of being
+saved.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import gemm as G
+from . import moe as M
+from . import mxfp4
+
+
+class ExpertWeights:
+    """Frozen MXFP4 expert projections of one layer (uint8 blocks/scales, fp32 biases).
+
+    ``dequantized()`` materialises bf16 [E, N, K] into a scratch buffer shared by all layers
+    of the same shape (one layer's MoE runs at a time on the compute stream)."""
+
+    _scratch: dict = {}
+
+    def __init__(self, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias):
+        self.gu_blocks, self.gu_scales, self.gu_bias = gu_blocks, gu_scales, gu_bias
+        self.dn_blocks, self.dn_scales, self.dn_bias = dn_blocks, dn_scales, dn_bias
+
+    @classmethod
+    def _buf(cls, key, shape, device):
+        k = (key, tuple(shape), str(device))
+        b = cls._scratch.get(k)
+        if b is None:
+            b = torch.empty(shape, device=device, dtype=torch.bfloat16)
+            cls._scratch[k] = b
+        return b
+
+    def gate_up(self) -> torch.Tensor:
+        E, N, Gk, _ = self.gu_blocks.shape
+        if not self.gu_blocks.is_cuda:
+            return mxfp4.dequantize(self.gu_blocks, self.gu_scales)
+        out = self._buf("gu", (E, N, Gk * 32), self.gu_blocks.device)
+        return mxfp4.dequantize(self.gu_blocks, self.gu_scales, out=out)
+
+    def down(self) -> torch.Tensor:
+        E, N, Gk, _ = self.dn_blocks.shape
+        if not self.dn_blocks.is_cuda:
+            return mxfp4.dequantize(self.dn_blocks, self.dn_scales)
+        out = self._buf("dn", (E, N, Gk * 32), self.dn_blocks.device)
+        return mxfp4.dequantize(self.dn_blocks, self.dn_scales, out=out)
+
+    @classmethod
+    def release_scratch(cls):
+        cls._scratch.clear()
+
+
+def _b(t):
+    return None if t is None else t.to(torch.bfloat16)
+
+
+class MoEFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xn, residual, router_w, router_b, gu_A, gu_B, dn_A, dn_B, experts,
+                top_k, replay_ids, s, act_alpha, act_limit, routing_out):
+        T, H = xn.shape
+        E = router_w.shape[0]
+        logits = G.matmul(xn, router_w, bias=router_b, out_dtype=torch.float32)
+        rt = M.route(logits, top_k, E, replay_ids=replay_ids)
+        if routing_out is not None:
+            routing_out.append(rt.ids)
+        x_s = M.gather_rows(xn, rt.row_src)
+        lora_gu = gu_A is not None
+        lora_dn = dn_A is not None
+        need_grad = torch.is_grad_enabled() or any(ctx.needs_input_grad)
+        W_gu = experts.gate_up()
+        xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if lora_gu else None
+        h, gu = G.grouped_matmul(x_s, W_gu, rt.offsets, epilogue="swiglu", bias=experts.gu_bias,
+                                 act_alpha=act_alpha, act_limit=act_limit,
+                                 save_preact=need_grad, a2=xa,
+                                 b2=_b(gu_B) if lora_gu else None)
+        W_dn = experts.down()
+        ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if lora_dn else None
+        y_s, _ = G.grouped_matmul(h, W_dn, rt.offsets, epilogue="rowscale", bias=experts.dn_bias,
+                                  row_scale=rt.row_gate, a2=ha,
+                                  b2=_b(dn_B) if lora_dn else None)
+        out = M.combine_rows(y_s, rt.dest, top_k, residual=residual)
+        ctx.experts = experts
+        ctx.cfg = (top_k, s, act_alpha, act_limit, lora_gu, lora_dn)
+        ctx.rt = rt
+        ctx.save_for_backward(xn, gu_A, gu_B, dn_A, dn_B, xa, h, ha, gu)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        xn, gu_A, gu_B, dn_A, dn_B, xa, h, ha, gu = ctx.saved_tensors
+        top_k, s, act_alpha, act_limit, lora_gu, lora_dn = ctx.cfg
+        rt = ctx.rt
+        experts = ctx.experts
+        dout = dout.contiguous()
+        g = M.gather_rows(dout, rt.row_src, rt.row_gate)            # gate * dout, [R, H]
+        W_dn = experts.down()                                       # [E, H, I] = (K=H, N=I)
+        d_dnA = d_dnB = d_guA = d_guB = None
+        if lora_dn:
+            gd = G.grouped_matmul(g, _b(dn_B), rt.offsets, b_layout="kn", alpha=s)[0]  # [R, r]
+            dgu, _ = G.grouped_matmul(g, W_dn, rt.offsets, b_layout="kn", epilogue="swiglu_bwd",
+                                      aux=gu, act_alpha=act_alpha, act_limit=act_limit,
+                                      a2=gd, b2=_b(dn_A))
+            d_dnA = G.grouped_k_matmul(gd, h, rt.offsets)                   # [E, r, I]
+            d_dnB = G.grouped_k_matmul(g, ha, rt.offsets)                   # [E, H, r]
+        else:
+            dgu, _ = G.grouped_matmul(g, W_dn, rt.offsets, b_layout="kn", epilogue="swiglu_bwd",
+                                      aux=gu, act_alpha=act_alpha, act_limit=act_limit)
+        del g
+        W_gu = experts.gate_up()                                    # [E, 2I, H] = (K=2I, N=H)
+        if lora_gu:
+            ga = G.grouped_matmul(dgu, _b(gu_B), rt.offsets, b_layout="kn", alpha=s)[0]
+            dx_s, _ = G.grouped_matmul(dgu, W_gu, rt.offsets, b_layout="kn", a2=ga,
+                                       b2=_b(gu_A))
+            x_s = M.gather_rows(xn, rt.row_src)
+            d_guA = G.grouped_k_matmul(ga, x_s, rt.offsets)                 # [E, r, H]
+            d_guB = G.grouped_k_matmul(dgu, xa, rt.offsets)                 # [E, 2I, r]
+        else:
+            dx_s, _ = G.grouped_matmul(dgu, W_gu, rt.offsets, b_layout="kn")
+        dxn = M.combine_rows(dx_s, rt.dest, top_k)
+        return (dxn, dout, None, None, d_guA, d_guB, d_dnA, d_dnB, None, None, None, None, None,
+                None, None)
+
+
+def moe_forward(xn, residual, router_w, router_b, experts: ExpertWeights, top_k: int,
+                lora: dict | None = None, s: float = 1.0, replay_ids=None,
+                act_alpha: float = 1.702, act_limit: float = 7.0, routing_out: list | None = None):
+    lora = lora or {}
+    return MoEFn.apply(xn, residual, router_w, router_b, lora.get("gu_A"), lora.get("gu_B"),
+                       lora.get("dn_A"), lora.get("dn_B"), experts, top_k, replay_ids, s,
+                       act_alpha, act_limit, routing_out)

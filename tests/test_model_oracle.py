@@ -1,0 +1,180 @@
+"""The gpt-oss implementation against Hugging Face transformers' own GptOss modeling (the
+CPU fp32 oracle of the tiny configuration), and LoRA gradients against plain autograd."""
+import pytest
+import torch
+
+from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
+from agent_factory_3_b200.models.gpt_oss.checkpoint import merged_state_dict
+from agent_factory_3_b200.ops import mxfp4
+
+
+def _hf_model(model: GptOssForCausalLM, merge_lora: bool):
+    from transformers import GptOssConfig as HFConfig
+    from transformers import GptOssForCausalLM as HFModel
+
+    cfg = model.cfg
+    hcfg = HFConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                    intermediate_size=cfg.intermediate_size,
+                    num_hidden_layers=cfg.num_hidden_layers,
+                    num_attention_heads=cfg.num_attention_heads,
+                    num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                    num_local_experts=cfg.num_local_experts,
+                    num_experts_per_tok=cfg.num_experts_per_tok,
+                    sliding_window=cfg.sliding_window, layer_types=cfg.layer_types,
+                    rope_parameters={"rope_type": "default", "rope_theta": cfg.rope_theta},
+                    max_position_embeddings=cfg.max_position_embeddings,
+                    rms_norm_eps=cfg.rms_norm_eps, attention_bias=True,
+                    tie_word_embeddings=False)
+    hcfg._attn_implementation = "eager"
+    hf = HFModel(hcfg).float().eval()
+    merged = merged_state_dict(model, dtype=torch.float32, attention_only=False) if merge_lora else {}
+    with torch.no_grad():
+        hf.model.embed_tokens.weight.copy_(model.embed_tokens.float())
+        hf.lm_head.weight.copy_(model.lm_head.float())
+        hf.model.norm.weight.copy_(model.norm)
+        q, kv = cfg.q_size, cfg.kv_size
+        for i, (hl, ml) in enumerate(zip(hf.model.layers, model.layers)):
+            a, m = ml.self_attn, ml.mlp
+            p = f"model.layers.{i}."
+            W = a.qkv_weight.float()
+            for name, lo, hi in (("q_proj", 0, q), ("k_proj", q, q + kv), ("v_proj", q + kv, q + 2 * kv)):
+                w = merged.get(p + f"self_attn.{name}.weight", W[lo:hi])
+                getattr(hl.self_attn, name).weight.copy_(w)
+                getattr(hl.self_attn, name).bias.copy_(a.qkv_bias[lo:hi])
+            hl.self_attn.o_proj.weight.copy_(merged.get(p + "self_attn.o_proj.weight", a.o_weight.float()))
+            hl.self_attn.o_proj.bias.copy_(a.o_bias)
+            hl.self_attn.sinks.copy_(a.sinks)
+            hl.input_layernorm.weight.copy_(ml.input_layernorm)
+            hl.post_attention_layernorm.weight.copy_(ml.post_attention_layernorm)
+            hl.mlp.router.weight.copy_(m.router_weight.float())
+            hl.mlp.router.bias.copy_(m.router_bias)
+            gu = merged.get(p + "mlp.experts.gate_up_proj",
+                            mxfp4.dequantize_reference(m.gate_up_blocks, m.gate_up_scales, torch.float32).transpose(1, 2))
+            dn = merged.get(p + "mlp.experts.down_proj",
+                            mxfp4.dequantize_reference(m.down_blocks, m.down_scales, torch.float32).transpose(1, 2))
+            hl.mlp.experts.gate_up_proj.copy_(gu)
+            hl.mlp.experts.gate_up_proj_bias.copy_(m.gate_up_bias)
+            hl.mlp.experts.down_proj.copy_(dn)
+            hl.mlp.experts.down_proj_bias.copy_(m.down_bias)
+    return hf
+
+
+def _model(lora=None, seed=0, dtype=torch.float32):
+    cfg = GptOssConfig.tiny()
+    m = GptOssForCausalLM(cfg, lora=lora, dtype=dtype).init_random(seed)
+    with torch.no_grad():  # non-trivial biases / norms so every term is exercised
+        g = torch.Generator().manual_seed(seed + 1)
+        for layer in m.layers:
+            layer.self_attn.qkv_bias.copy_(torch.randn(layer.self_attn.qkv_bias.shape, generator=g) * 0.02)
+            layer.self_attn.o_bias.copy_(torch.randn(layer.self_attn.o_bias.shape, generator=g) * 0.02)
+            layer.mlp.gate_up_bias.copy_(torch.randn(layer.mlp.gate_up_bias.shape, generator=g) * 0.02)
+            layer.mlp.down_bias.copy_(torch.randn(layer.mlp.down_bias.shape, generator=g) * 0.02)
+            layer.input_layernorm.copy_(1 + torch.randn(64, generator=g) * 0.1)
+            for name, p in list(layer.self_attn.lora.items()) + list(layer.mlp.lora.items()):
+                if name.endswith("_B"):
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.05)
+    m.gradient_checkpointing = False
+    return m
+
+
+def _packed(seqlens, vocab, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, vocab, (sum(seqlens),), generator=g)
+    pos = torch.cat([torch.arange(n) for n in seqlens])
+    cu = torch.tensor([0] + list(torch.tensor(seqlens).cumsum(0)), dtype=torch.int32)
+    return ids, pos, cu
+
+
+@pytest.mark.parametrize("use_lora", [False, True])
+def test_forward_matches_hf(use_lora):
+    lora = LoraConfig(r=8, lora_alpha=16, target_modules=["q_proj", "k_proj", "v_proj", "o_proj",
+                                                           "gate_up_proj", "down_proj"]) if use_lora else None
+    m = _model(lora)
+    hf = _hf_model(m, merge_lora=use_lora)
+    seqlens = [40, 23]
+    ids, pos, cu = _packed(seqlens, m.cfg.vocab_size)
+    with torch.no_grad():
+        h = m.forward_hidden(ids, pos, cu)
+        logits = m.logits(h)
+        ref = []
+        for s, e in zip(cu[:-1].tolist(), cu[1:].tolist()):
+            ref.append(hf(input_ids=ids[s:e][None]).logits[0])
+        ref = torch.cat(ref)
+    err = (logits - ref).abs().max().item()
+    assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
+
+
+def test_routing_replay_reproduces_routing():
+    m = _model()
+    ids, pos, cu = _packed([30, 17], m.cfg.vocab_size, seed=3)
+    with torch.no_grad():
+        h1, rec = m.forward_hidden(ids, pos, cu, record_routing=True)
+        h2 = m.forward_hidden(ids, pos, cu, routing_indices=rec)
+        # replaying different indices changes the output
+        h3 = m.forward_hidden(ids, pos, cu, routing_indices=(rec + 1) % m.cfg.num_local_experts)
+    assert rec.shape == (47, 2, 2)
+    torch.testing.assert_close(h1, h2)
+    assert (h1 - h3).abs().max() > 1e-3
+
+
+def test_lora_grads_match_autograd():
+    lora = LoraConfig(r=4, lora_alpha=8, target_modules=["q_proj", "v_proj", "o_proj",
+                                                           "gate_up_proj", "down_proj"])
+    m = _model(lora, seed=5)
+    ids, pos, cu = _packed([25, 12], m.cfg.vocab_size, seed=6)
+    labels = torch.roll(ids, -1)
+    h = m.forward_hidden(ids, pos, cu)
+    lp, ent = m.token_logprobs(h, labels)
+    (lp.sum() * -1.0 + 0.1 * ent.sum()).backward()
+    grads = {n: p.grad.clone() for n, p in m.named_parameters() if p.requires_grad}
+    assert grads and all(g is not None for g in grads.values())
+
+    # independent autograd: HF model whose weights are W + s*B@A built from leaf A/B
+    from torch.func import functional_call
+    hf = _hf_model(m, merge_lora=False)
+    params = {n: p.detach().clone().requires_grad_(True) for n, p in m.named_parameters() if p.requires_grad}
+    cfg = m.cfg
+    q, kv = cfg.q_size, cfg.kv_size
+    s = lora.scaling
+    overrides = {}
+    for i, ml in enumerate(m.layers):
+        a, mm = ml.self_attn, ml.mlp
+        pre = f"layers.{i}."
+        W = a.qkv_weight.float()
+        for name, lo, hi in (("q_proj", 0, q), ("k_proj", q, q + kv), ("v_proj", q + kv, q + 2 * kv)):
+            w = W[lo:hi]
+            if f"{pre}self_attn.lora.{name}_A" in params:
+                w = w + s * params[f"{pre}self_attn.lora.{name}_B"] @ params[f"{pre}self_attn.lora.{name}_A"]
+            overrides[f"model.layers.{i}.self_attn.{name}.weight"] = w
+        w = a.o_weight.float() + s * params[f"{pre}self_attn.lora.o_proj_B"] @ params[f"{pre}self_attn.lora.o_proj_A"]
+        overrides[f"model.layers.{i}.self_attn.o_proj.weight"] = w
+        gu = mxfp4.dequantize_reference(mm.gate_up_blocks, mm.gate_up_scales, torch.float32)
+        gu = gu + s * torch.bmm(params[f"{pre}mlp.lora.gu_B"], params[f"{pre}mlp.lora.gu_A"])
+        dn = mxfp4.dequantize_reference(mm.down_blocks, mm.down_scales, torch.float32)
+        dn = dn + s * torch.bmm(params[f"{pre}mlp.lora.dn_B"], params[f"{pre}mlp.lora.dn_A"])
+        overrides[f"model.layers.{i}.mlp.experts.gate_up_proj"] = gu.transpose(1, 2)
+        overrides[f"model.layers.{i}.mlp.experts.down_proj"] = dn.transpose(1, 2)
+    # the reference propagates no gradient through the routing weights: detach router scores
+    for hl in hf.model.layers:
+        router = hl.mlp.router
+        orig = router.forward
+
+        def fwd(x, _orig=orig):
+            logits, scores, idx = _orig(x)
+            return logits, scores.detach(), idx
+
+        router.forward = fwd
+    hf_logits = []
+    for st, en in zip(cu[:-1].tolist(), cu[1:].tolist()):
+        out = functional_call(hf, overrides, args=(), kwargs={"input_ids": ids[st:en][None]})
+        hf_logits.append(out.logits[0])
+    logits = torch.cat(hf_logits)
+    logp = torch.log_softmax(logits, -1)
+    lp_ref = logp.gather(-1, labels[:, None]).squeeze(-1)
+    ent_ref = -(logp.exp() * logp).sum(-1)
+    torch.testing.assert_close(lp.detach(), lp_ref.detach(), rtol=2e-3, atol=2e-3)
+    (lp_ref.sum() * -1.0 + 0.1 * ent_ref.sum()).backward()
+    for n, g in grads.items():
+        ref = params[n].grad
+        err = (g - ref).abs().max().item()
+        assert err <= 1e-2 * (ref.abs().max().item() + 1e-6), (n, err, ref.abs().max().item())
