@@ -1,0 +1,463 @@
+// Flash-attention backward for gpt-oss on sm_100a (causal GQA, packed varlen, sliding
+// window, learned sinks, head_dim 64).
+//
+// One CTA per (128-key tile, kv head).  It keeps K and V of its key tile in shared memory and
+// loops over every q head of the kv group and every 128-query block that can see the tile:
+//   S^T  = K Q^T        (tcgen05, M=128 keys, N=128 queries, K=64)     TMEM cols   0..127
+//   dP^T = V dO^T       (same shape)                                  TMEM cols 128..255
+//   P^T  = 2^(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - D[q])   (softmax warps,
+//          thread = key row, written as bf16 into 128B-swizzled shared memory)
+//   dV  += P^T dO       (A = P^T K-major, B = dO as MN-major)         TMEM cols 256..319
+//   dK  += dS^T Q       (A = dS^T, B = Q as MN-major)                 TMEM cols 320..383
+//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..447
+// dQ of each block is added to an fp32 buffer with 16-byte vector atomics; dK and dV are
+// complete at the end of the CTA (all q heads of the group were visited) and are written once
+// as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the sink gradient
+// d(sink_h) = -sum_i exp(sink_h - lse_h(i)) * D_h(i); an epilogue kernel converts dQ to bf16.
+#include "common.h"
+#include "host_utils.h"
+#include "sm100.cuh"
+
+namespace af3 {
+namespace attnb {
+
+constexpr int kThreads = 256;
+constexpr int kHD = 64;
+constexpr int kB = 128;  // keys per CTA tile, queries per block
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Smem {
+  static constexpr int K = 0;                         // 16 KB  [128 keys x 64] K-major
+  static constexpr int V = K + kB * kHD * 2;          // 16 KB
+  static constexpr int QDO = V + kB * kHD * 2;        // 2 stages x (Q 16 KB + dO 16 KB)
+  static constexpr int PT = QDO + 2 * 2 * kB * kHD * 2;   // 32 KB P^T
+  static constexpr int DST = PT + kB * kB * 2;        // 32 KB dS^T
+  static constexpr int LD = DST + kB * kB * 2;        // 2 stages x (lse2 512 B + D 512 B)
+  static constexpr int BAR = LD + 2 * 2 * kB * 4;
+  static constexpr int TOTAL = BAR + 1024;
+};
+
+struct Params {
+  const int* tiles;   // [n, 4] (seq_start, seq_end, k_start, k_end)
+  const float* lse;   // [Hq, T] natural log
+  const float* Dd;    // [Hq, T]
+  float* dq;          // [T, Hq*64] fp32 accumulator
+  __nv_bfloat16* dqkv;
+  int64_t ld_dqkv;
+  int T, hq, hkv, window;
+  float scale, scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void store_sw128(uint8_t* base, int row, int c8, uint4 w) {
+  // element (row, 8*c8 .. 8*c8+7) of a [128 rows x 128 cols] bf16 K-major SW128 tile made of
+  // two 64-column blocks of 16 KB
+  const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
+  *reinterpret_cast<uint4*>(base + blk * 16384 + row * 128 + ch * 16) = w;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tma_qkv,
+                    const __grid_constant__ CUtensorMap tma_do, const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* ld_full = bars + 5;    // [2]
+  uint64_t* ld_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_empty = bars + 10;
+  uint64_t* p_full = bars + 11;
+  uint64_t* mma_done = bars + 12;  // P/dS smem free and dQ ready
+  uint64_t* dq_empty = bars + 13;
+  uint64_t* final_done = bars + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int g = blockIdx.x;  // kv head
+  const int tile = blockIdx.y;
+  const int seq1 = p.tiles[tile * 4 + 1];
+  const int k0 = p.tiles[tile * 4 + 2];
+  const int k1 = p.tiles[tile * 4 + 3];
+  if (k1 <= k0) return;
+  const int rep = p.hq / p.hkv;
+  int q_end = seq1;
+  if (p.window > 0) q_end = min(seq1, k1 - 1 + p.window);
+  const int nqb = (q_end - k0 + kB - 1) / kB;
+  const int n_it = rep * nqb;  // (q head, query block) pairs
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_qkv);
+    tma_prefetch_desc(&tma_do);
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+      mbar_init(&ld_full[s], 32);
+      mbar_init(&ld_empty[s], 128);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 128);
+    mbar_init(p_full, 128);
+    mbar_init(mma_done, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(final_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer ------------------------------------
+    if (elect_one_sync()) {
+      mbar_arrive_expect_tx(kv_full, 2 * kB * kHD * 2);
+      tma_load_2d(smem + Smem::K, &tma_qkv, kv_full, (p.hq + g) * kHD, k0);
+      tma_load_2d(smem + Smem::V, &tma_qkv, kv_full, (p.hq + p.hkv + g) * kHD, k0);
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&qdo_empty[s], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) break;
+        const int h = g * rep + it / nqb;
+        const int qb = k0 + (it % nqb) * kB;
+        uint8_t* q = smem + Smem::QDO + s * 2 * kB * kHD * 2;
+        mbar_arrive_expect_tx(&qdo_full[s], 2 * kB * kHD * 2);
+        tma_load_2d(q, &tma_qkv, &qdo_full[s], h * kHD, qb);
+        tma_load_2d(q + kB * kHD * 2, &tma_do, &qdo_full[s], h * kHD, qb);
+      }
+    }
+  } else if (warp == 3) {
+    // ---------------------- lse / D loader (plain loads) -----------------------------
+    for (int it = 0; it < n_it; ++it) {
+      const int s = it & 1;
+      if (!mbar_wait(&ld_empty[s], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) break;
+      const int h = g * rep + it / nqb;
+      const int qb = k0 + (it % nqb) * kB;
+      float* dst = reinterpret_cast<float*>(smem + Smem::LD + s * 2 * kB * 4);
+      for (int c = lane; c < kB; c += 32) {
+        const int qi = qb + c;
+        const bool ok = qi < p.T;
+        dst[c] = ok ? p.lse[(int64_t)h * p.T + qi] * kLog2e : INFINITY;
+        dst[kB + c] = ok ? p.Dd[(int64_t)h * p.T + qi] : 0.f;
+      }
+      mbar_arrive(&ld_full[s]);
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer --------------------------------------
+    if (elect_one_sync()) {
+      constexpr uint32_t id_s = make_idesc_bf16(kB, kB, false, false);      // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_bf16(kB, kHD, false, true);     // dV, dK
+      constexpr uint32_t id_q = make_idesc_bf16(kB, kHD, true, true);       // dQ
+      const uint32_t sK = smem_u32(smem + Smem::K), sV = smem_u32(smem + Smem::V);
+      const uint32_t sPT = smem_u32(smem + Smem::PT), sDS = smem_u32(smem + Smem::DST);
+      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag);
+      for (int it = 0; ok && it <= n_it; ++it) {
+        if (it < n_it) {
+          const int s = it & 1;
+          if (!mbar_wait(&qdo_full[s], (it >> 1) & 1, p.err, abort_flag)) break;
+          if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
+          const uint32_t sDO = sQ + kB * kHD * 2;
+#pragma unroll
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            umma_f16(tmem + 0, make_smem_desc(sK + kk * 32, 16, 1024, kLayoutSW128),
+                     make_smem_desc(sQ + kk * 32, 16, 1024, kLayoutSW128), id_s, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            umma_f16(tmem + 128, make_smem_desc(sV + kk * 32, 16, 1024, kLayoutSW128),
+                     make_smem_desc(sDO + kk * 32, 16, 1024, kLayoutSW128), id_s, kk > 0);
+          }
+          umma_commit(s_full);
+        }
+        if (it >= 1) {
+          const int j = it - 1;
+          const int s = j & 1;
+          if (!mbar_wait(p_full, j & 1, p.err, abort_flag)) break;
+          if (!mbar_wait(dq_empty, (j & 1) ^ 1, p.err, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
+          const uint32_t sDO = sQ + kB * kHD * 2;
+#pragma unroll
+          for (int kk = 0; kk < kB / 16; ++kk) {
+            // reduction over the 128 queries of the block
+            const uint64_t a_pt = make_smem_desc(sPT + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024,
+                                                 kLayoutSW128);
+            const uint64_t a_ds = make_smem_desc(sDS + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024,
+                                                 kLayoutSW128);
+            const uint64_t b_do = make_smem_desc(sDO + kk * 2048, 8192, 1024, kLayoutSW128);
+            const uint64_t b_q = make_smem_desc(sQ + kk * 2048, 8192, 1024, kLayoutSW128);
+            umma_f16(tmem + 256, a_pt, b_do, id_kv, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem + 320, a_ds, b_q, id_kv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kB / 16; ++kk) {
+            // reduction over the 128 keys: A = dS (M = queries) read from dS^T as MN-major
+            const uint64_t a = make_smem_desc(sDS + kk * 2048, 16384, 1024, kLayoutSW128);
+            const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
+            umma_f16(tmem + 384, a, b, id_q, kk > 0);
+          }
+          umma_commit(mma_done);
+          umma_commit(&qdo_empty[s]);
+        }
+      }
+      if (ok) umma_commit(final_done);
+    }
+  } else if (warp >= 4) {
+    // ------------------------- softmax-gradient / epilogue ---------------------------
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;          // key row (S^T) or query row (dQ)
+    const uint32_t lb = (uint32_t)(qd * 32) << 16;
+    const int key = k0 + r;
+    bool ok = true;
+    for (int it = 0; it <= n_it && ok; ++it) {
+      if (it >= 1) {
+        // dQ of block it-1 (also frees P^T / dS^T shared memory)
+        const int j = it - 1;
+        if (!mbar_wait(mma_done, j & 1, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const int h = g * rep + j / nqb;
+        const int qi = k0 + (j % nqb) * kB + r;
+        uint32_t v0[32], v1[32];
+        tmem_ld_32x32b_x32(tmem + lb + 384, v0);
+        tmem_ld_32x32b_x32(tmem + lb + 416, v1);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+        if (qi < q_end) {
+          float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            atomicAdd(dst + c, make_float4(__uint_as_float(v0[4 * c]) * p.scale,
+                                           __uint_as_float(v0[4 * c + 1]) * p.scale,
+                                           __uint_as_float(v0[4 * c + 2]) * p.scale,
+                                           __uint_as_float(v0[4 * c + 3]) * p.scale));
+            atomicAdd(dst + 8 + c, make_float4(__uint_as_float(v1[4 * c]) * p.scale,
+                                               __uint_as_float(v1[4 * c + 1]) * p.scale,
+                                               __uint_as_float(v1[4 * c + 2]) * p.scale,
+                                               __uint_as_float(v1[4 * c + 3]) * p.scale));
+          }
+        }
+      }
+      if (it < n_it) {
+        const int s = it & 1;
+        if (!mbar_wait(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(s_full, it & 1, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const float* lse2 = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);
+        const float* Dq = lse2 + kB;
+        const int qb = k0 + (it % nqb) * kB;
+        uint8_t* pt = smem + Smem::PT;
+        uint8_t* ds = smem + Smem::DST;
+#pragma unroll 1
+        for (int c = 0; c < kB; c += 32) {
+          uint32_t sv[32], dv[32];
+          tmem_ld_32x32b_x32(tmem + lb + c, sv);
+          tmem_ld_32x32b_x32(tmem + lb + 128 + c, dv);
+          tmem_ld_wait();
+          if (c + 32 == kB) {
+            tc_fence_before();
+            mbar_arrive(s_empty);
+          }
+          float pr[32], dsr[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qi = qb + c + e;
+            const bool vis = key < k1 && key <= qi && qi < q_end &&
+                             (p.window == 0 || qi - key < p.window);
+            const float pv = vis ? ex2(__uint_as_float(sv[e]) * p.scale_log2 - lse2[c + e]) : 0.f;
+            pr[e] = pv;
+            dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
+          }
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 w, z;
+            w.x = pack_bf16x2(pr[q8 * 8 + 0], pr[q8 * 8 + 1]);
+            w.y = pack_bf16x2(pr[q8 * 8 + 2], pr[q8 * 8 + 3]);
+            w.z = pack_bf16x2(pr[q8 * 8 + 4], pr[q8 * 8 + 5]);
+            w.w = pack_bf16x2(pr[q8 * 8 + 6], pr[q8 * 8 + 7]);
+            z.x = pack_bf16x2(dsr[q8 * 8 + 0], dsr[q8 * 8 + 1]);
+            z.y = pack_bf16x2(dsr[q8 * 8 + 2], dsr[q8 * 8 + 3]);
+            z.z = pack_bf16x2(dsr[q8 * 8 + 4], dsr[q8 * 8 + 5]);
+            z.w = pack_bf16x2(dsr[q8 * 8 + 6], dsr[q8 * 8 + 7]);
+            store_sw128(pt, r, c / 8 + q8, w);
+            store_sw128(ds, r, c / 8 + q8, z);
+          }
+        }
+        mbar_arrive(&ld_empty[s]);
+        fence_proxy_async_smem();
+        mbar_arrive(p_full);
+      }
+    }
+    if (ok && mbar_wait(final_done, 0, p.err, abort_flag)) {
+      tc_fence_after();
+      uint32_t a0[32], a1[32], b0[32], b1[32];
+      tmem_ld_32x32b_x32(tmem + lb + 256, a0);   // dV
+      tmem_ld_32x32b_x32(tmem + lb + 288, a1);
+      tmem_ld_32x32b_x32(tmem + lb + 320, b0);   // dK
+      tmem_ld_32x32b_x32(tmem + lb + 352, b1);
+      tmem_ld_wait();
+      if (key < k1) {
+        __nv_bfloat16* dk = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + g) * kHD;
+        __nv_bfloat16* dv = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + p.hkv + g) * kHD;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 0]) * p.scale, __uint_as_float(b0[c8 * 8 + 1]) * p.scale);
+          w.y = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 2]) * p.scale, __uint_as_float(b0[c8 * 8 + 3]) * p.scale);
+          w.z = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 4]) * p.scale, __uint_as_float(b0[c8 * 8 + 5]) * p.scale);
+          w.w = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 6]) * p.scale, __uint_as_float(b0[c8 * 8 + 7]) * p.scale);
+          reinterpret_cast<uint4*>(dk)[c8] = w;
+          w.x = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 0]) * p.scale, __uint_as_float(b1[c8 * 8 + 1]) * p.scale);
+          w.y = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 2]) * p.scale, __uint_as_float(b1[c8 * 8 + 3]) * p.scale);
+          w.z = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 4]) * p.scale, __uint_as_float(b1[c8 * 8 + 5]) * p.scale);
+          w.w = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 6]) * p.scale, __uint_as_float(b1[c8 * 8 + 7]) * p.scale);
+          reinterpret_cast<uint4*>(dk)[4 + c8] = w;
+          w.x = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 0]), __uint_as_float(a0[c8 * 8 + 1]));
+          w.y = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 2]), __uint_as_float(a0[c8 * 8 + 3]));
+          w.z = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 4]), __uint_as_float(a0[c8 * 8 + 5]));
+          w.w = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 6]), __uint_as_float(a0[c8 * 8 + 7]));
+          reinterpret_cast<uint4*>(dv)[c8] = w;
+          w.x = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 0]), __uint_as_float(a1[c8 * 8 + 1]));
+          w.y = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 2]), __uint_as_float(a1[c8 * 8 + 3]));
+          w.z = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 4]), __uint_as_float(a1[c8 * 8 + 5]));
+          w.w = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 6]), __uint_as_float(a1[c8 * 8 + 7]));
+          reinterpret_cast<uint4*>(dv)[4 + c8] = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// D[h, i] = sum_d dO[i, h, d] * O[i, h, d]; dsink[h] -= exp(sink_h - lse[h, i]) * D[h, i].
+// One warp per (row, head) pair; head_dim 64 = 2 elements per lane.
+__global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, int64_t ld_out,
+                                    const __nv_bfloat16* __restrict__ dout, int64_t ld_dout,
+                                    const float* __restrict__ lse, const float* __restrict__ sinks,
+                                    float* __restrict__ Dd, float* __restrict__ dsink, int T,
+                                    int hq) {
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (w >= (int64_t)T * hq) return;
+  const int h = (int)(w % hq);
+  const int64_t i = w / hq;
+  const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(out + i * ld_out + h * kHD)[lane];
+  const __nv_bfloat162 d = reinterpret_cast<const __nv_bfloat162*>(dout + i * ld_dout + h * kHD)[lane];
+  const float2 of = __bfloat1622float2(o), df = __bfloat1622float2(d);
+  float s = of.x * df.x + of.y * df.y;
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffff, s, k);
+  if (lane == 0) {
+    Dd[(int64_t)h * T + i] = s;
+    atomicAdd(&dsink[h], -__expf(sinks[h] - lse[(int64_t)h * T + i]) * s);
+  }
+}
+
+// dqkv[:, q part] = bf16(dq)
+__global__ void attn_bwd_post_kernel(const float* __restrict__ dq, __nv_bfloat16* __restrict__ dqkv,
+                                     int64_t ld, int64_t T, int qcols) {
+  const int64_t n = T * qcols / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(dq)[i];
+    const int64_t row = (i * 4) / qcols, col = (i * 4) % qcols;
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(dqkv + row * ld + col);
+    o[0] = __floats2bfloat162_rn(v.x, v.y);
+    o[1] = __floats2bfloat162_rn(v.z, v.w);
+  }
+}
+
+}  // namespace attnb
+
+void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, torch::Tensor cu,
+              torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
+              torch::Tensor dsinks, int64_t hq, int64_t hkv, int64_t d, int64_t window,
+              double scale) {
+  using namespace attnb;
+  check_cuda_bf16(qkv, "qkv");
+  check_cuda_bf16(dout, "dout");
+  check_cuda_bf16(dqkv, "dqkv");
+  AF3_CHECK(d == kHD, "attention backward is built for head_dim 64");
+  AF3_CHECK(dout.stride(1) == 1 && out.stride(1) == 1 && dqkv.stride(1) == 1, "unit inner strides");
+  AF3_CHECK(kv_tiles.size(1) == 4, "kv_tiles must be [n, 4]");
+  const int64_t T = qkv.size(0);
+  const int64_t n_tiles = kv_tiles.size(0);
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  if (T == 0 || n_tiles == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto Dd = torch::empty({hq, T}, qkv.options().dtype(torch::kFloat32));
+  auto dq = torch::zeros({T, hq * kHD}, qkv.options().dtype(torch::kFloat32));
+  {
+    const int64_t warps = T * hq;
+    attn_bwd_pre_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+        lse.data_ptr<float>(), sinks.data_ptr<float>(), Dd.data_ptr<float>(),
+        dsinks.data_ptr<float>(), (int)T, (int)hq);
+    AF3_CUDA_CHECK(cudaGetLastError());
+  }
+  const uint64_t dims[2] = {(uint64_t)qkv.size(1), (uint64_t)T};
+  const uint64_t strides[1] = {(uint64_t)qkv.stride(0) * 2};
+  const uint32_t box[2] = {64, 128};
+  CUtensorMap tq = make_tmap(qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, strides,
+                             box, CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint64_t ddims[2] = {(uint64_t)dout.size(1), (uint64_t)T};
+  const uint64_t dstrides[1] = {(uint64_t)dout.stride(0) * 2};
+  CUtensorMap tdo = make_tmap(dout.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ddims,
+                              dstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  Params p;
+  p.tiles = kv_tiles.data_ptr<int>();
+  p.lse = lse.data_ptr<float>();
+  p.Dd = Dd.data_ptr<float>();
+  p.dq = dq.data_ptr<float>();
+  p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.ld_dqkv = dqkv.stride(0);
+  p.T = (int)T;
+  p.hq = (int)hq;
+  p.hkv = (int)hkv;
+  p.window = (int)window;
+  p.scale = (float)scale;
+  p.scale_log2 = (float)scale * kLog2e;
+  p.err = device_error_ptr();
+  const int smem = Smem::TOTAL + 1024;
+  static bool attr[64] = {};
+  int dev;
+  AF3_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!attr[dev]) {
+    AF3_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev] = true;
+  }
+  dim3 grid((unsigned)hkv, (unsigned)n_tiles);
+  attn_bwd_kernel<<<grid, kThreads, smem, stream>>>(tq, tdo, p);
+  AF3_CUDA_CHECK(cudaGetLastError());
+  const int64_t n4 = T * hq * kHD / 4;
+  attn_bwd_post_kernel<<<std::min<int64_t>((n4 + 255) / 256, num_sms() * 16), 256, 0, stream>>>(
+      dq.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0), T,
+      (int)(hq * kHD));
+  AF3_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace af3

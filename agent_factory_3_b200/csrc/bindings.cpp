@@ -36,6 +36,13 @@ void lse_merge(torch::Tensor parts, torch::Tensor label_logit, torch::Tensor log
 void swiglu_fwd(torch::Tensor gu, torch::Tensor out, double alpha, double limit);
 void swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu, double alpha,
                 double limit);
+void attn_fwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor tiles, torch::Tensor cu,
+              torch::Tensor out, torch::Tensor lse, int64_t hq, int64_t hkv, int64_t d,
+              int64_t window, double scale);
+void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, torch::Tensor cu,
+              torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
+              torch::Tensor dsinks, int64_t hq, int64_t hkv, int64_t d, int64_t window,
+              double scale);
 }  // namespace af3
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -61,6 +68,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lse_merge", &af3::lse_merge);
   m.def("swiglu_fwd", &af3::swiglu_fwd);
   m.def("swiglu_bwd", &af3::swiglu_bwd);
+  m.def("attn_fwd", &af3::attn_fwd);
+  m.def("attn_bwd", &af3::attn_bwd);
   m.def("device_error", &af3::device_error_take,
         "Read and clear the current device's kernel error word (0 = no error).");
 }

@@ -104,20 +104,22 @@ class AttentionPlan:
     """Host-built tile lists for one packed batch (reused by every layer of a step).
 
     tiles: int32 [n, 3] = (seq_start, q_start, q_end) query tiles of 128 rows, heaviest first;
-    kv_tiles: int32 [m, 3] = (seq_start, k_start, k_end) key tiles for the backward pass."""
+    kv_tiles: int32 [m, 4] = (seq_start, seq_end, k_start, k_end) key tiles for the backward
+    pass, heaviest (most queries after them) first."""
 
     BLOCK = 128
 
     def __init__(self, cu_seqlens: torch.Tensor, device):
         cu = [int(x) for x in cu_seqlens.tolist()]
-        tiles = []
+        tiles, kv = [], []
         for s, e in zip(cu[:-1], cu[1:]):
             for q0 in range(s, e, self.BLOCK):
                 tiles.append((s, q0, min(q0 + self.BLOCK, e)))
+                kv.append((s, e, q0, min(q0 + self.BLOCK, e)))
         order = sorted(tiles, key=lambda t: -(t[2] - t[0]))  # longest causal prefix first
         self.tiles = torch.tensor(order or [(0, 0, 0)], dtype=torch.int32, device=device)
-        self.kv_tiles = torch.tensor(sorted(tiles, key=lambda t: t[1] - t[0]) or [(0, 0, 0)],
-                                     dtype=torch.int32, device=device)
+        kv_order = sorted(kv, key=lambda t: -(t[1] - t[2]))   # most later queries first
+        self.kv_tiles = torch.tensor(kv_order or [(0, 0, 0, 0)], dtype=torch.int32, device=device)
         self.cu = torch.tensor(cu, dtype=torch.int32, device=device)
         self.n_tiles = len(tiles)
 
@@ -129,7 +131,7 @@ def kernel_available() -> bool:
     global _HAS_KERNEL
     if _HAS_KERNEL is None:
         try:
-            _HAS_KERNEL = hasattr(ext(), "attn_fwd")
+            _HAS_KERNEL = hasattr(ext(), "attn_fwd") and hasattr(ext(), "attn_bwd")
         except RuntimeError:
             _HAS_KERNEL = False
     return _HAS_KERNEL
