@@ -192,12 +192,13 @@ class GptOssForCausalLM(nn.Module):
         (Kaiming-uniform like PEFT), LoRA B zero."""
         cfg = self.cfg
         std = cfg.initializer_range if std is None else std
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        dev = self.embed_tokens.device
+        # generate where the weights live: a 120b init on the GPU takes seconds
+        g = torch.Generator(device=dev).manual_seed(seed)
 
         def randn(*shape):
-            return torch.randn(*shape, generator=g) * std
+            return torch.randn(*shape, generator=g, device=dev) * std
 
-        dev = self.embed_tokens.device
         self.embed_tokens.copy_(randn(*self.embed_tokens.shape).to(dev))
         self.lm_head.copy_(randn(*self.lm_head.shape).to(dev))
         for layer in self.layers:
@@ -220,7 +221,21 @@ class GptOssForCausalLM(nn.Module):
                 for name, p in mod.lora.items():
                     if name.endswith("_A"):
                         bound = 1.0 / math.sqrt(p.shape[-1])
-                        p.copy_((torch.rand(*p.shape, generator=g) * 2 - 1).mul_(bound).to(dev))
+                        p.copy_((torch.rand(*p.shape, generator=g, device=dev) * 2 - 1).mul_(bound))
+                    else:
+                        p.zero_()
+        return self
+
+    @torch.no_grad()
+    def init_lora(self, seed: int = 0) -> "GptOssForCausalLM":
+        """PEFT-style LoRA init only (A uniform(-1/sqrt(in), 1/sqrt(in)), B = 0)."""
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        for layer in self.layers:
+            for mod in (layer.self_attn, layer.mlp):
+                for name, p in mod.lora.items():
+                    if name.endswith("_A"):
+                        bound = 1.0 / math.sqrt(p.shape[-1])
+                        p.copy_((torch.rand(*p.shape, generator=g) * 2 - 1).mul_(bound).to(p.device))
                     else:
                         p.zero_()
         return self

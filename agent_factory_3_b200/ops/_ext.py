@@ -14,6 +14,35 @@ import torch
 _EXT = None
 _ERR: Exception | None = None
 
+# Kernel launches issued by each extension entry point (for the launch counter below).
+_LAUNCHES_PER_CALL = {"moe_group": 4, "attn_bwd": 3, "device_error": 0}
+_launch_count = 0
+
+
+class _CountingExt:
+    """Proxy of the extension module that counts the kernels its entry points launch."""
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        n = _LAUNCHES_PER_CALL.get(name, 1)
+
+        def call(*a, **k):
+            global _launch_count
+            _launch_count += n
+            return fn(*a, **k)
+
+        return call
+
+
+def launch_count() -> int:
+    """Number of this package's kernels launched so far in this process."""
+    return _launch_count
+
 
 def ext():
     """Return the compiled extension module, importing it on first use."""
@@ -26,7 +55,7 @@ def ext():
             "`python setup.py build_ext --inplace`"
         ) from _ERR
     try:
-        _EXT = importlib.import_module("agent_factory_3_b200._C")
+        _EXT = _CountingExt(importlib.import_module("agent_factory_3_b200._C"))
     except Exception as e:  # pragma: no cover - exercised on machines without the build
         _ERR = e
         raise RuntimeError(

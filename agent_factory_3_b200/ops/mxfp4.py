@@ -56,8 +56,9 @@ def quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     e = torch.ceil(torch.log2(amax / 6.0)).clamp(-127, 127)
     scale = torch.pow(2.0, e)
     y = (x / scale).clamp(-6.0, 6.0)
-    mags = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], device=w.device)
-    idx = (y.abs().unsqueeze(-1) - mags).abs().argmin(dim=-1)
+    # nearest E2M1 magnitude {0, .5, 1, 1.5, 2, 3, 4, 6} via the midpoints between them
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], device=w.device)
+    idx = torch.bucketize(y.abs(), mids)
     code = idx + (y < 0).to(idx.dtype) * 8
     code = torch.where(idx == 0, torch.zeros_like(code), code)
     code = code.to(torch.uint8).reshape(*code.shape[:-1], 16, 2)
