@@ -1,0 +1,147 @@
+"""Micro-benchmarks of the sm_100a kernels, timed with CUDA events after warm-up.
+
+    python -m agent_factory_3_b200.benchmarks.kernels --op attn_fwd --seqlens 8192 --iters 10
+    python -m agent_factory_3_b200.benchmarks.kernels --op attn_bwd --seqlens 8192
+    python -m agent_factory_3_b200.benchmarks.kernels --op gemm --m 16384 --n 5760 --k 2880
+    python -m agent_factory_3_b200.benchmarks.kernels --op moe --tokens 32768
+
+Each run prints one JSON line with the time per call, the achieved TFLOP/s (or GB/s) and the
+fraction of the measured peak in MEASURED_PEAKS.json (when present).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+
+def _peaks():
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    except OSError:
+        return 1590.0, 6650.0, "fallback"
+
+
+def _time(fn, iters, warmup=3, flush_bytes=0):
+    flush = torch.empty(flush_bytes // 4, dtype=torch.float32, device="cuda") if flush_bytes else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def attention_flops(seqlens, hq, d, window, bwd=False):
+    f = 0
+    for L in seqlens:
+        if window:
+            pairs = sum(min(i + 1, window) for i in range(L))
+        else:
+            pairs = L * (L + 1) // 2
+        f += 4 * pairs * d * hq
+    return f * (2.5 if bwd else 1.0)
+
+
+def bench_attention(args, bwd):
+    from ..ops import attention as A
+    hq, hkv, d = args.hq, args.hkv, 64
+    seqlens = [int(x) for x in args.seqlens.split(",")]
+    T = sum(seqlens)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    sinks = torch.randn(hq, device="cuda")
+    cu = torch.tensor([0] + torch.tensor(seqlens).cumsum(0).tolist(), dtype=torch.int32)
+    plan = A.AttentionPlan(cu, "cuda")
+    out = torch.empty(T, hq * d, device="cuda").bfloat16()
+    lse = torch.empty(hq, T, device="cuda")
+    scale = 1 / math.sqrt(d)
+    ext = A.ext()
+
+    def fwd():
+        ext.attn_fwd(qkv, sinks, plan.tiles, plan.cu, out, lse, hq, hkv, d, args.window, scale)
+
+    if not bwd:
+        ms = _time(fwd, args.iters)
+    else:
+        fwd()
+        dout = torch.randn_like(out)
+        dqkv = torch.empty_like(qkv)
+        ds = torch.zeros(hq, device="cuda")
+
+        def b():
+            ext.attn_bwd(qkv, sinks, plan.kv_tiles, plan.cu, out, dout, lse, dqkv, ds, hq, hkv, d,
+                         args.window, scale)
+
+        ms = _time(b, args.iters)
+    fl = attention_flops(seqlens, hq, d, args.window, bwd)
+    return {"flops": fl, "ms": ms}
+
+
+def bench_gemm(args):
+    from ..ops import gemm as G
+    a = torch.randn(args.m, args.k, device="cuda").bfloat16()
+    b = torch.randn(args.n, args.k, device="cuda").bfloat16()
+    out = torch.empty(args.m, args.n, device="cuda").bfloat16()
+    ms = _time(lambda: G.matmul(a, b, out=out), args.iters)
+    return {"flops": 2 * args.m * args.n * args.k, "ms": ms}
+
+
+def bench_moe(args):
+    from ..ops import moe as M
+    from ..ops import gemm as G
+    E, K, H, I = 128, 4, 2880, 2880
+    T = args.tokens
+    logits = torch.randn(T, E, device="cuda")
+    rt = M.route(logits, K, E)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    xs = M.gather_rows(x, rt.row_src)
+    W = (torch.randn(E, 2 * I, H, device="cuda") * 0.02).bfloat16()
+    bias = torch.zeros(E, 2 * I, device="cuda")
+    ms = _time(lambda: G.grouped_matmul(xs, W, rt.offsets, epilogue="swiglu", bias=bias), args.iters)
+    return {"flops": 2 * T * K * 2 * I * H, "ms": ms}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe"])
+    ap.add_argument("--seqlens", default="8192")
+    ap.add_argument("--hq", type=int, default=64)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--window", type=int, default=0)
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=5760)
+    ap.add_argument("--k", type=int, default=2880)
+    ap.add_argument("--tokens", type=int, default=32768)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    if args.op == "attn_fwd":
+        r = bench_attention(args, False)
+    elif args.op == "attn_bwd":
+        r = bench_attention(args, True)
+    elif args.op == "gemm":
+        r = bench_gemm(args)
+    else:
+        r = bench_moe(args)
+    peak_tf, _, kind = _peaks()
+    tf = r["flops"] / (r["ms"] / 1e3) / 1e12
+    print(json.dumps({"op": args.op, "ms": round(r["ms"], 4), "tflops": round(tf, 1),
+                      f"frac_of_{kind}_bf16_peak": round(tf / peak_tf, 3), "args": vars(args)}))
+
+
+if __name__ == "__main__":
+    main()

@@ -54,6 +54,10 @@ class GptOssConfig:
             self.layer_types = _alternating_layer_types(self.num_hidden_layers)
         assert len(self.layer_types) == self.num_hidden_layers
         assert self.hidden_size % 32 == 0 and self.intermediate_size % 32 == 0
+        for name in ("pad_token_id", "eos_token_id"):
+            v = getattr(self, name)
+            if not 0 <= v < self.vocab_size:
+                raise ValueError(f"{name}={v} is outside the vocabulary (size {self.vocab_size})")
 
     # ---- derived sizes ----
     @property

@@ -17,7 +17,11 @@ from ..types import TrainingSample
 
 
 class DataCollatorWithPacking:
-    def __init__(self, pad_token_id: int = 0, pad_to_multiple_of: int = 128, pin_memory: bool = False):
+    def __init__(self, pad_token_id: int = 0, pad_to_multiple_of: int = 128, pin_memory: bool = False,
+                 vocab_size: int | None = None):
+        if vocab_size is not None and not 0 <= pad_token_id < vocab_size:
+            raise ValueError(f"pad_token_id {pad_token_id} outside vocabulary of {vocab_size}")
+        self.vocab_size = vocab_size
         self.pad_token_id = pad_token_id
         self.pad_to_multiple_of = pad_to_multiple_of
         self.pin_memory = pin_memory
@@ -39,6 +43,8 @@ class DataCollatorWithPacking:
             return out
 
         ids = pack("input_ids", np.int64, self.pad_token_id)
+        if self.vocab_size is not None and T and (ids.min() < 0 or ids.max() >= self.vocab_size):
+            raise ValueError(f"token id outside [0, {self.vocab_size}) in the batch")
         pos = np.empty(T, dtype=np.int64)
         seg = np.empty(T, dtype=np.int64)
         off = 0

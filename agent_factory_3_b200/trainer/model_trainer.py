@@ -100,7 +100,8 @@ class ModelTrainer(RPCMixin):
                                         entropy_top_pct=config.entropy_top_pct)
         self.collator = DataCollatorWithPacking(pad_token_id=self.model.cfg.pad_token_id,
                                                 pad_to_multiple_of=config.pad_to_multiple_of_training,
-                                                pin_memory=self.device.type == "cuda")
+                                                pin_memory=self.device.type == "cuda",
+                                                vocab_size=self.model.cfg.vocab_size)
         self.step_count = 0
         self.last_step_events = None
         RPCMixin.__init__(self, group=rpc_group)
