@@ -21,7 +21,7 @@
 namespace af3 {
 namespace attnb {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 8..11 drain dQ from TMEM
 constexpr int kHD = 64;
 constexpr int kB = 128;  // keys per CTA tile, queries per block
 constexpr float kLog2e = 1.4426950408889634f;
@@ -30,11 +30,11 @@ struct Smem {
   static constexpr int K = 0;                         // 16 KB  [128 keys x 64] K-major
   static constexpr int V = K + kB * kHD * 2;          // 16 KB
   static constexpr int QDO = V + kB * kHD * 2;        // 2 stages x (Q 16 KB + dO 16 KB)
-  static constexpr int PT = QDO + 2 * 2 * kB * kHD * 2;   // 32 KB P^T
-  static constexpr int DST = PT + kB * kB * 2;        // 32 KB dS^T
-  static constexpr int LD = DST + kB * kB * 2;        // 2 stages x (lse2 512 B + D 512 B)
+  static constexpr int PT = QDO + 2 * 2 * kB * kHD * 2;   // 2 x 32 KB P^T (double buffered)
+  static constexpr int DST = PT + 2 * kB * kB * 2;    // 2 x 32 KB dS^T
+  static constexpr int LD = DST + 2 * kB * kB * 2;    // 2 stages x (lse2 512 B + D 512 B)
   static constexpr int BAR = LD + 2 * 2 * kB * 4;
-  static constexpr int TOTAL = BAR + 1024;
+  static constexpr int TOTAL = BAR + 1024;            // 227 KB: the whole per-CTA budget
 };
 
 struct Params {
@@ -66,8 +66,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tma_qkv,
                     const __grid_constant__ CUtensorMap tma_do, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // the layout uses all 227 KB, so there is no slack to realign: require a 1024-aligned base
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023) != 0) {
+    if (threadIdx.x == 0) atomicExch(p.err, kErrBadShape);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::BAR);
   uint64_t* kv_full = bars + 0;
   uint64_t* qdo_full = bars + 1;   // [2]
@@ -76,11 +80,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* ld_empty = bars + 7;   // [2]
   uint64_t* s_full = bars + 9;
   uint64_t* s_empty = bars + 10;
-  uint64_t* p_full = bars + 11;
-  uint64_t* mma_done = bars + 12;  // P/dS smem free and dQ ready
-  uint64_t* dq_empty = bars + 13;
-  uint64_t* final_done = bars + 14;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* p_full = bars + 11;    // [2] P^T/dS^T buffer b written
+  uint64_t* mma_done = bars + 13;  // [2] P^T/dS^T buffer b consumed
+  uint64_t* dq_full = bars + 15;   // [2]
+  uint64_t* dq_empty = bars + 17;  // [2]
+  uint64_t* final_done = bars + 19;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -108,9 +113,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(s_empty, 128);
-    mbar_init(p_full, 128);
-    mbar_init(mma_done, 1);
-    mbar_init(dq_empty, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 128);
+      mbar_init(&mma_done[b], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_empty[s], 128);
+    }
     mbar_init(final_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -189,18 +199,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it >= 1) {
           const int j = it - 1;
           const int s = j & 1;
-          if (!mbar_wait(p_full, j & 1, p.err, abort_flag)) break;
-          if (!mbar_wait(dq_empty, (j & 1) ^ 1, p.err, abort_flag)) break;
+          if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
+          if (!mbar_wait(&dq_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err, abort_flag)) break;
           tc_fence_after();
           const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
           const uint32_t sDO = sQ + kB * kHD * 2;
+          const uint32_t sPTb = sPT + (j & 1) * kB * kB * 2;
+          const uint32_t sDSb = sDS + (j & 1) * kB * kB * 2;
 #pragma unroll
           for (int kk = 0; kk < kB / 16; ++kk) {
             // reduction over the 128 queries of the block
-            const uint64_t a_pt = make_smem_desc(sPT + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024,
-                                                 kLayoutSW128);
-            const uint64_t a_ds = make_smem_desc(sDS + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024,
-                                                 kLayoutSW128);
+            const uint64_t a_pt = make_smem_desc(sPTb + (kk / 4) * 16384 + (kk % 4) * 32, 16,
+                                                 1024, kLayoutSW128);
+            const uint64_t a_ds = make_smem_desc(sDSb + (kk / 4) * 16384 + (kk % 4) * 32, 16,
+                                                 1024, kLayoutSW128);
             const uint64_t b_do = make_smem_desc(sDO + kk * 2048, 8192, 1024, kLayoutSW128);
             const uint64_t b_q = make_smem_desc(sQ + kk * 2048, 8192, 1024, kLayoutSW128);
             umma_f16(tmem + 256, a_pt, b_do, id_kv, (j > 0 || kk > 0) ? 1u : 0u);
@@ -209,38 +221,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kB / 16; ++kk) {
             // reduction over the 128 keys: A = dS (M = queries) read from dS^T as MN-major
-            const uint64_t a = make_smem_desc(sDS + kk * 2048, 16384, 1024, kLayoutSW128);
+            const uint64_t a = make_smem_desc(sDSb + kk * 2048, 16384, 1024, kLayoutSW128);
             const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
-            umma_f16(tmem + 384, a, b, id_q, kk > 0);
+            umma_f16(tmem + 384 + (j & 1) * kHD, a, b, id_q, kk > 0);
           }
-          umma_commit(mma_done);
+          umma_commit(&mma_done[j & 1]);
+          umma_commit(&dq_full[j & 1]);
           umma_commit(&qdo_empty[s]);
         }
       }
       if (ok) umma_commit(final_done);
     }
-  } else if (warp >= 4) {
-    // ------------------------- softmax-gradient / epilogue ---------------------------
+  } else if (warp >= 8) {
+    // ------------------------- dQ drain (TMEM -> fp32 atomics) ------------------------
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;          // key row (S^T) or query row (dQ)
+    const int r = qd * 32 + lane;  // query row of the block
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
-    const int key = k0 + r;
-    bool ok = true;
-    for (int it = 0; it <= n_it && ok; ++it) {
-      if (it >= 1) {
-        // dQ of block it-1 (also frees P^T / dS^T shared memory)
-        const int j = it - 1;
-        if (!mbar_wait(mma_done, j & 1, p.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const int h = g * rep + j / nqb;
-        const int qi = k0 + (j % nqb) * kB + r;
-        uint32_t v0[32], v1[32];
-        tmem_ld_32x32b_x32(tmem + lb + 384, v0);
-        tmem_ld_32x32b_x32(tmem + lb + 416, v1);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(dq_empty);
-        if (qi < q_end) {
+    for (int j = 0; j < n_it; ++j) {
+      if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
+      tc_fence_after();
+      const int h = g * rep + j / nqb;
+      const int qi = k0 + (j % nqb) * kB + r;
+      uint32_t v0[32], v1[32];
+      tmem_ld_32x32b_x32(tmem + lb + 384 + (j & 1) * kHD, v0);
+      tmem_ld_32x32b_x32(tmem + lb + 416 + (j & 1) * kHD, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&dq_empty[j & 1]);
+      if (qi < q_end) {
           float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -253,9 +261,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                __uint_as_float(v1[4 * c + 2]) * p.scale,
                                                __uint_as_float(v1[4 * c + 3]) * p.scale));
           }
-        }
       }
-      if (it < n_it) {
+    }
+  } else if (warp >= 4) {
+    // --------------------------- softmax gradient (P^T, dS^T) ---------------------------
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;  // key row of S^T
+    const uint32_t lb = (uint32_t)(qd * 32) << 16;
+    const int key = k0 + r;
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      {
+        // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
+        if (it >= 2 && !mbar_wait(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
         const int s = it & 1;
         if (!mbar_wait(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
         if (!mbar_wait(s_full, it & 1, p.err, abort_flag)) { ok = false; break; }
@@ -263,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* lse2 = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);
         const float* Dq = lse2 + kB;
         const int qb = k0 + (it % nqb) * kB;
-        uint8_t* pt = smem + Smem::PT;
-        uint8_t* ds = smem + Smem::DST;
+        uint8_t* pt = smem + Smem::PT + (it & 1) * kB * kB * 2;
+        uint8_t* ds = smem + Smem::DST + (it & 1) * kB * kB * 2;
 #pragma unroll 1
         for (int c = 0; c < kB; c += 32) {
           uint32_t sv[32], dv[32];
@@ -276,14 +297,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(s_empty);
           }
           float pr[32], dsr[32];
+          // every query of this 32-column chunk visible from this key row?
+          const bool all_vis = key < k1 && key <= qb + c && qb + c + 31 < q_end &&
+                               (p.window == 0 || qb + c + 31 - key < p.window);
+          if (all_vis) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qi = qb + c + e;
-            const bool vis = key < k1 && key <= qi && qi < q_end &&
-                             (p.window == 0 || qi - key < p.window);
-            const float pv = vis ? ex2(__uint_as_float(sv[e]) * p.scale_log2 - lse2[c + e]) : 0.f;
-            pr[e] = pv;
-            dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
+            for (int e = 0; e < 32; ++e) {
+              const float pv = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -lse2[c + e]));
+              pr[e] = pv;
+              dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int qi = qb + c + e;
+              const bool vis = key < k1 && key <= qi && qi < q_end &&
+                               (p.window == 0 || qi - key < p.window);
+              const float pv =
+                  vis ? ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -lse2[c + e])) : 0.f;
+              pr[e] = pv;
+              dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
+            }
           }
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8) {
@@ -302,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive(&ld_empty[s]);
         fence_proxy_async_smem();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[it & 1]);
       }
     }
     if (ok && mbar_wait(final_done, 0, p.err, abort_flag)) {
@@ -441,7 +475,7 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
   p.scale = (float)scale;
   p.scale_log2 = (float)scale * kLog2e;
   p.err = device_error_ptr();
-  const int smem = Smem::TOTAL + 1024;
+  const int smem = Smem::TOTAL;
   static bool attr[64] = {};
   int dev;
   AF3_CUDA_CHECK(cudaGetDevice(&dev));

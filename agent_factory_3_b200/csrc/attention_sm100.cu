@@ -202,12 +202,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_ld_32x32b_x32(ta + 64, r2);
           tmem_ld_32x32b_x32(ta + 96, r3);
           tmem_ld_wait();
+          // raw scores; the softmax scale is applied inside the exp2 argument (one FFMA)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            sv[e] = __uint_as_float(r0[e]) * p.scale_log2;
-            sv[32 + e] = __uint_as_float(r1[e]) * p.scale_log2;
-            sv[64 + e] = __uint_as_float(r2[e]) * p.scale_log2;
-            sv[96 + e] = __uint_as_float(r3[e]) * p.scale_log2;
+            sv[e] = __uint_as_float(r0[e]);
+            sv[32 + e] = __uint_as_float(r1[e]);
+            sv[64 + e] = __uint_as_float(r2[e]);
+            sv[96 + e] = __uint_as_float(r3[e]);
           }
         }
         tc_fence_before();
@@ -224,12 +225,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!vis) sv[c] = -INFINITY;
           }
         }
-        float mx = m_run;
+        // row max as a tree of independent chains (raw score units)
+        float mxp[8];
 #pragma unroll
-        for (int c = 0; c < kBKV; ++c) mx = fmaxf(mx, sv[c]);
+        for (int t = 0; t < 8; ++t) mxp[t] = sv[t];
+#pragma unroll
+        for (int c = 8; c < kBKV; c += 8) {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) mxp[t] = fmaxf(mxp[t], sv[c + t]);
+        }
+        float mraw = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                           fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        const float mx = fmaxf(m_run, mraw * p.scale_log2);
         const float m_use = (mx == -INFINITY) ? 0.f : mx;
         const float alpha = ex2(m_run - m_use);  // m_run = -inf -> 0
-        float rs = 0.f;
+        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         // P_j -> shared memory (bf16, 128B swizzle, two 64-key column blocks)
         uint8_t* prow = pbase + (j & 1) * kBQ * kBKV * 2 + row * 128;
 #pragma unroll
@@ -237,8 +247,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float pv[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            pv[e] = ex2(sv[c8 * 8 + e] - m_use);
-            rs += pv[e];
+            pv[e] = ex2(fmaf(sv[c8 * 8 + e], p.scale_log2, -m_use));
+            rsp[e] += pv[e];
           }
           uint4 w;
           w.x = pack_bf16x2(pv[0], pv[1]);
@@ -248,6 +258,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
           *reinterpret_cast<uint4*>(prow + blk * 16384 + ch * 16) = w;
         }
+        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
         l_run = l_run * alpha + rs;
         m_run = mx;
         m_hist[j & 1] = m_use;

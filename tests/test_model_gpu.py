@@ -15,7 +15,8 @@ def small_cfg():
     return GptOssConfig(vocab_size=4096, hidden_size=256, intermediate_size=256,
                         num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
                         head_dim=64, num_local_experts=8, num_experts_per_tok=2,
-                        sliding_window=32, rope_scaling=None, max_position_embeddings=4096)
+                        sliding_window=32, rope_scaling=None, max_position_embeddings=4096,
+                        pad_token_id=0, eos_token_id=1)
 
 
 def test_dual_gemm(dev):
