@@ -273,6 +273,7 @@ def main():
                     "api": "ModelTrainer.train_packed_batch"},
             "gpu_launches": int(launches),
             "init_s": round(t_init, 1),
+            "max_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1),
             "loss": losses[-1],
         }
         print(json.dumps(out), flush=True)
