@@ -43,6 +43,17 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
               torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
               torch::Tensor dsinks, int64_t hq, int64_t hkv, int64_t d, int64_t window,
               double scale);
+void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages,
+                      torch::Tensor page_table, torch::Tensor seq_lens, torch::Tensor sinks,
+                      torch::Tensor out, c10::optional<torch::Tensor> lse, int64_t hq, int64_t hkv,
+                      int64_t window, double scale, int64_t max_seq_len);
+void kv_store(torch::Tensor qkv, int64_t k_off, int64_t v_off, torch::Tensor slots,
+              torch::Tensor k_pages, torch::Tensor v_pages);
+void kv_gather(torch::Tensor qkv, int64_t k_off, int64_t v_off, torch::Tensor slots,
+               torch::Tensor k_pages, torch::Tensor v_pages);
+void sample_tokens(torch::Tensor logits, torch::Tensor temperature, c10::optional<torch::Tensor> min_p,
+                   torch::Tensor seeds, int64_t step, torch::Tensor tokens, torch::Tensor logprobs,
+                   torch::Tensor entropy);
 }  // namespace af3
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -70,6 +81,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &af3::swiglu_bwd);
   m.def("attn_fwd", &af3::attn_fwd);
   m.def("attn_bwd", &af3::attn_bwd);
+  m.def("decode_attention", &af3::decode_attention);
+  m.def("kv_store", &af3::kv_store);
+  m.def("kv_gather", &af3::kv_gather);
+  m.def("sample_tokens", &af3::sample_tokens);
   m.def("device_error", &af3::device_error_take,
         "Read and clear the current device's kernel error word (0 = no error).");
 }

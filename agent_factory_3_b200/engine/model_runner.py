@@ -1,0 +1,162 @@
+"""Forward pass of the rollout engine over a mixed batch of prefill chunks and decode tokens.
+
+All new tokens of a step are packed into one row block so every projection and MoE GEMM runs
+once per layer for the whole batch.  Attention splits by kind:
+  * decode tokens (one new token on top of cached pages) -> paged decode attention kernel;
+  * prefill chunks -> the packed flash-attention kernel on a buffer holding each sequence's
+    full context (cached K/V gathered from pages, queries only for the new rows; the tile list
+    covers just the new rows).
+New K/V go straight into their page slots; the MoE expert ids chosen for every new token are
+written next to them so routed experts can be returned for prefix-cache hits later.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from ..models.gpt_oss.model import GptOssForCausalLM
+from ..ops import decode as D
+from ..ops._ext import ext, use_cuda_kernels
+from ..ops.attention import attention_reference
+from ..ops.gemm import matmul
+from ..ops.linear import block_diag_b, lora_linear
+from ..ops.norm import rmsnorm
+from ..ops.rope import apply_rope_
+from .kv_cache import PagedKVCache
+
+
+@dataclass
+class StepItem:
+    ids: list[int]          # new tokens
+    start: int              # number of tokens already in the cache for this sequence
+    pages: list[int]        # pages covering start + len(ids) tokens
+    want_logits: bool = True
+
+
+@dataclass
+class StepOutput:
+    logits: torch.Tensor            # [n_items, V] fp32 (last new token of each item)
+    routing: torch.Tensor | None    # [N, L, K] uint8 of the new tokens
+    item_rows: list[tuple[int, int]] = field(default_factory=list)
+
+
+class ModelRunner:
+    def __init__(self, model: GptOssForCausalLM, kv: PagedKVCache, lora_active: bool = True):
+        self.model = model
+        self.kv = kv
+        self.cfg = model.cfg
+        self.lora_active = lora_active
+        self.device = model.embed_tokens.device
+        self._bd_cache: dict = {}
+
+    def _qkv_lora(self, attn):
+        if not self.lora_active:
+            return None, None
+        return attn._qkv_lora()
+
+    @torch.inference_mode()
+    def forward(self, items: list[StepItem]) -> StepOutput:
+        cfg = self.cfg
+        dev = self.device
+        P = self.kv.page_size
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        qs, kvs = cfg.q_size, cfg.kv_size
+        ids, pos, slots, rows = [], [], [], []
+        dec_idx, pre_idx = [], []
+        for i, it in enumerate(items):
+            n = len(it.ids)
+            r0 = len(ids)
+            ids += it.ids
+            for j in range(n):
+                p = it.start + j
+                pos.append(p)
+                slots.append(it.pages[p // P] * P + p % P)
+            rows.append((r0, r0 + n))
+            (dec_idx if (n == 1 and it.start > 0) else pre_idx).append(i)
+        N = len(ids)
+        ids_t = torch.tensor(ids, device=dev, dtype=torch.long)
+        pos_t = torch.tensor(pos, device=dev, dtype=torch.int32)
+        slots_t = torch.tensor(slots, device=dev, dtype=torch.int32)
+        # decode metadata
+        if dec_idx:
+            maxp = max(len(items[i].pages) for i in dec_idx)
+            pt = torch.zeros(len(dec_idx), maxp, dtype=torch.int32)
+            for r, i in enumerate(dec_idx):
+                pt[r, :len(items[i].pages)] = torch.tensor(items[i].pages, dtype=torch.int32)
+            dec_pt = pt.to(dev)
+            dec_lens = torch.tensor([items[i].start + 1 for i in dec_idx], device=dev, dtype=torch.int32)
+            dec_rows = torch.tensor([rows[i][0] for i in dec_idx], device=dev, dtype=torch.long)
+            dec_max = int(max(items[i].start + 1 for i in dec_idx))
+        # prefill metadata: packed full contexts
+        if pre_idx:
+            ctx_slots, new_in_ctx, new_rows, tiles, cu = [], [], [], [], [0]
+            for i in pre_idx:
+                it = items[i]
+                L = it.start + len(it.ids)
+                base = cu[-1]
+                for p in range(L):
+                    ctx_slots.append(it.pages[p // P] * P + p % P)
+                new_in_ctx += list(range(base + it.start, base + L))
+                new_rows += list(range(*rows[i]))
+                for q0 in range(it.start, L, 128):
+                    tiles.append((base, base + q0, base + min(q0 + 128, L)))
+                cu.append(base + L)
+            tiles.sort(key=lambda t: -(t[2] - t[0]))
+            ctx_slots_t = torch.tensor(ctx_slots, device=dev, dtype=torch.int32)
+            new_in_ctx_t = torch.tensor(new_in_ctx, device=dev, dtype=torch.long)
+            new_rows_t = torch.tensor(new_rows, device=dev, dtype=torch.long)
+            tiles_t = torch.tensor(tiles, device=dev, dtype=torch.int32)
+            cu_t = torch.tensor(cu, device=dev, dtype=torch.int32)
+            n_ctx = cu[-1]
+        cos, sin = self.model.rope(dev)
+        x = torch.nn.functional.embedding(ids_t, self.model.embed_tokens)
+        rec: list = []
+        scale = 1.0 / math.sqrt(d)
+        for li, layer in enumerate(self.model.layers):
+            a, m = layer.self_attn, layer.mlp
+            xn = rmsnorm(x, layer.input_layernorm, cfg.rms_norm_eps)
+            A, B = self._qkv_lora(a)
+            qkv = lora_linear(xn, a.qkv_weight, a.qkv_bias, A, B, None, a.lora_scaling)
+            apply_rope_(qkv, hq + hkv, d, pos_t, cos, sin)
+            kp, vp = self.kv.k[li], self.kv.v[li]
+            D.kv_store(qkv, qs, qs + kvs, slots_t, kp, vp)
+            o = torch.empty(N, qs, device=dev, dtype=qkv.dtype)
+            if dec_idx:
+                q = qkv.index_select(0, dec_rows)
+                od = D.decode_attention(q[:, :qs], kp, vp, dec_pt, dec_lens, a.sinks, hq, hkv,
+                                        a.window, scale, dec_max)
+                o.index_copy_(0, dec_rows, od)
+            if pre_idx:
+                ctx = torch.zeros(n_ctx, qkv.shape[1], device=dev, dtype=qkv.dtype)
+                D.kv_gather(ctx, qs, qs + kvs, ctx_slots_t, kp, vp)
+                ctx.index_copy_(0, new_in_ctx_t, qkv.index_select(0, new_rows_t))
+                if use_cuda_kernels(ctx) and d == 64:
+                    oc = torch.empty(n_ctx, qs, device=dev, dtype=qkv.dtype)
+                    lse = torch.empty(hq, n_ctx, device=dev, dtype=torch.float32)
+                    ext().attn_fwd(ctx, a.sinks.float().contiguous(), tiles_t, cu_t, oc, lse, hq,
+                                   hkv, d, a.window, scale)
+                else:
+                    oc = attention_reference(ctx, cu_t, a.sinks, hq, hkv, d, a.window, scale)
+                o.index_copy_(0, new_rows_t, oc.index_select(0, new_in_ctx_t))
+            oA = a.lora["o_proj_A"] if (self.lora_active and "o_proj_A" in a.lora) else None
+            oB = a.lora["o_proj_B"] if (self.lora_active and "o_proj_B" in a.lora) else None
+            h = lora_linear(o, a.o_weight, a.o_bias, oA, oB, x, a.lora_scaling)
+            hn = rmsnorm(h, layer.post_attention_layernorm, cfg.rms_norm_eps)
+            lay_rec: list = []
+            if self.lora_active:
+                x = m(hn, h, None, lay_rec)
+            else:
+                from ..ops.moe_layer import moe_forward
+                x = moe_forward(hn, h, m.router_weight, m.router_bias, m.experts(),
+                                cfg.num_experts_per_tok, None, 1.0, None, cfg.swiglu_alpha,
+                                cfg.swiglu_limit, lay_rec)
+            rec.append(lay_rec[0])
+        routing = torch.stack(rec, dim=1).to(torch.uint8)       # [N, L, K]
+        self.kv.routing.view(-1, cfg.num_hidden_layers, cfg.num_experts_per_tok)[slots_t.long()] = routing
+        last = torch.tensor([r[1] - 1 for r, it in zip(rows, items) if it.want_logits],
+                            device=dev, dtype=torch.long)
+        hl = rmsnorm(x.index_select(0, last), self.model.norm, cfg.rms_norm_eps)
+        logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
+        return StepOutput(logits=logits, routing=routing, item_rows=rows)

@@ -1,0 +1,193 @@
+"""sglang-compatible HTTP server of the rollout engine.
+
+Endpoints (contract of the sglang API the reference drives, see rollout/llm_backend/
+sglang_backend.py and trainer/sglang_controller.py of agent-factory-3):
+  POST /generate                 input_ids, sampling_params, stream, return_logprob,
+                                 logprob_start_len, return_entropy, top_logprobs_num,
+                                 return_routed_experts, lora_path, extra_key
+  POST /pause_generation         {"mode": "abort" | "in_place"}
+  POST /continue_generation
+  POST /load_lora_adapter        {"lora_name", "lora_path"}
+  POST /unload_lora_adapter      {"lora_name"}
+  POST /update_weight_version    {"new_version"}
+  POST /flush_cache
+  POST /update_weights_from_disk {"model_path", "flush_cache", "weight_version"}
+  GET  /v1/loads, /health, /get_model_info, /get_server_info
+Control calls return once the engine thread has applied them, so a weight sync needs no
+fixed sleeps (the reference sleeps >= 13 s per LoRA sync waiting for sglang's asynchronous
+scheduler).
+
+    python -m agent_factory_3_b200.engine.server --model gpt-oss-120b --port 30000
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import logging
+
+from aiohttp import web
+
+from .scheduler import Engine, Request
+
+logger = logging.getLogger(__name__)
+
+
+def _request_from_json(body: dict) -> Request:
+    sp = body.get("sampling_params") or {}
+    ids = body.get("input_ids")
+    if not isinstance(ids, list) or not ids:
+        raise web.HTTPBadRequest(text="input_ids must be a non-empty list of token ids")
+    return Request(
+        input_ids=[int(t) for t in ids], max_new_tokens=int(sp.get("max_new_tokens", 128)),
+        temperature=float(sp.get("temperature", 1.0)), top_p=float(sp.get("top_p", 1.0)),
+        top_k=int(sp.get("top_k", -1)), min_p=float(sp.get("min_p") or 0.0),
+        seed=sp.get("sampling_seed"), stop_token_ids=[int(t) for t in sp.get("stop_token_ids") or []],
+        return_logprob=bool(body.get("return_logprob", False)),
+        return_entropy=bool(body.get("return_entropy", False)),
+        top_logprobs_num=int(body.get("top_logprobs_num") or 0),
+        return_routed_experts=bool(body.get("return_routed_experts", False)),
+        lora_path=body.get("lora_path"), extra_key=body.get("extra_key"),
+        stream=bool(body.get("stream", False)))
+
+
+def build_app(engine: Engine, model_info: dict | None = None) -> web.Application:
+    app = web.Application(client_max_size=1 << 30)
+
+    async def generate(request: web.Request):
+        body = await request.json()
+        req = _request_from_json(body)
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        req.on_output = lambda out: loop.call_soon_threadsafe(q.put_nowait, out)
+        engine.submit(req)
+        if not req.stream:
+            while True:
+                out = await q.get()
+                if out["finished"]:
+                    return web.json_response({"output_ids": out["output_ids"],
+                                              "meta_info": out["meta_info"]})
+        resp = web.StreamResponse(headers={"Content-Type": "text/event-stream",
+                                           "Cache-Control": "no-cache"})
+        await resp.prepare(request)
+        try:
+            while True:
+                out = await q.get()
+                chunk = {"output_ids": out["output_ids"], "meta_info": out["meta_info"]}
+                await resp.write(f"data: {json.dumps(chunk)}\n\n".encode())
+                if out["finished"]:
+                    break
+            await resp.write(b"data: [DONE]\n\n")
+        except (ConnectionResetError, asyncio.CancelledError):
+            pass
+        return resp
+
+    def control(cmd, *args):
+        return asyncio.get_running_loop().run_in_executor(None, lambda: engine.control(cmd, *args))
+
+    async def pause(request):
+        body = await request.json() if request.can_read_body else {}
+        await control("pause", body.get("mode", "abort"))
+        return web.json_response({"success": True})
+
+    async def cont(request):
+        await control("continue")
+        return web.json_response({"success": True})
+
+    async def load_lora(request):
+        body = await request.json()
+        try:
+            await control("load_lora", body["lora_name"], body["lora_path"])
+        except Exception as e:  # noqa: BLE001
+            return web.json_response({"success": False, "message": str(e)}, status=400)
+        return web.json_response({"success": True})
+
+    async def unload_lora(request):
+        body = await request.json()
+        if body.get("lora_name") not in engine.loras:
+            return web.json_response({"success": False,
+                                      "message": f"LoRA adapter {body.get('lora_name')} does not exist"},
+                                     status=400)
+        await control("unload_lora", body["lora_name"])
+        return web.json_response({"success": True})
+
+    async def weight_version(request):
+        body = await request.json()
+        await control("update_weight_version", body.get("new_version"))
+        return web.json_response({"success": True})
+
+    async def flush(request):
+        try:
+            await control("flush_cache")
+        except Exception as e:  # noqa: BLE001
+            return web.json_response({"success": False, "message": str(e)}, status=400)
+        return web.json_response({"success": True})
+
+    async def update_weights(request):
+        body = await request.json()
+        await control("update_weights", body["model_path"], bool(body.get("flush_cache", True)))
+        if body.get("weight_version") is not None:
+            await control("update_weight_version", body["weight_version"])
+        return web.json_response({"success": True, "message": "weights updated"})
+
+    async def loads(request):
+        return web.json_response({"loads": [engine.loads()]})
+
+    async def health(request):
+        return web.Response(text="ok")
+
+    async def info(request):
+        return web.json_response(model_info or {"model": "gpt-oss"})
+
+    app.router.add_post("/generate", generate)
+    app.router.add_post("/pause_generation", pause)
+    app.router.add_post("/continue_generation", cont)
+    app.router.add_post("/load_lora_adapter", load_lora)
+    app.router.add_post("/unload_lora_adapter", unload_lora)
+    app.router.add_post("/update_weight_version", weight_version)
+    app.router.add_post("/flush_cache", flush)
+    app.router.add_post("/update_weights_from_disk", update_weights)
+    app.router.add_get("/v1/loads", loads)
+    app.router.add_get("/health", health)
+    app.router.add_get("/get_model_info", info)
+    app.router.add_get("/get_server_info", info)
+    return app
+
+
+def main():
+    import torch
+
+    from ..models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
+    from ..models.gpt_oss.checkpoint import load_checkpoint
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="gpt-oss-120b", help="preset name or checkpoint directory")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=30000)
+    ap.add_argument("--num-pages", type=int, default=8192)
+    ap.add_argument("--page-size", type=int, default=64)
+    ap.add_argument("--max-running-requests", type=int, default=128)
+    ap.add_argument("--max-prefill-tokens", type=int, default=16384)
+    ap.add_argument("--lora-r", type=int, default=0, help="LoRA capacity (0 = no LoRA serving)")
+    ap.add_argument("--lora-targets", default="q_proj,k_proj,v_proj,o_proj")
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args()
+    from pathlib import Path
+    p = Path(a.model)
+    cfg = GptOssConfig.load(p / "config.json") if (p / "config.json").exists() else GptOssConfig.preset(a.model)
+    lora = LoraConfig(r=a.lora_r, lora_alpha=2 * a.lora_r, target_modules=a.lora_targets.split(",")) if a.lora_r else None
+    model = GptOssForCausalLM(cfg, lora=lora, device="cuda")
+    if p.is_dir():
+        load_checkpoint(p, model)
+    else:
+        model.init_random(a.seed)
+    model.eval()
+    eng = Engine(model, num_pages=a.num_pages, page_size=a.page_size,
+                 max_running=a.max_running_requests, max_prefill_tokens=a.max_prefill_tokens).start()
+    web.run_app(build_app(eng, {"model": a.model, "num_hidden_layers": cfg.num_hidden_layers,
+                                "num_experts_per_tok": cfg.num_experts_per_tok}),
+                host=a.host, port=a.port)
+    torch.cuda.synchronize()
+
+
+if __name__ == "__main__":
+    main()

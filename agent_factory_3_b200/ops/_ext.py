@@ -15,7 +15,7 @@ _EXT = None
 _ERR: Exception | None = None
 
 # Kernel launches issued by each extension entry point (for the launch counter below).
-_LAUNCHES_PER_CALL = {"moe_group": 4, "attn_bwd": 3, "device_error": 0}
+_LAUNCHES_PER_CALL = {"moe_group": 4, "attn_bwd": 3, "decode_attention": 2, "device_error": 0}
 _launch_count = 0
 
 

@@ -1,0 +1,177 @@
+"""Rollout engine on the tiny model (CPU reference kernels; the same code drives the sm_100a
+kernels on GPU): greedy decoding equals a full recompute, prefix caching, routed experts,
+pause/abort/continue, LoRA hot-swap and merged-weight reload through the HTTP API."""
+import asyncio
+import base64
+
+import numpy as np
+import pytest
+import torch
+from aiohttp.test_utils import TestClient, TestServer
+
+from agent_factory_3_b200.engine.kv_cache import PagedKVCache
+from agent_factory_3_b200.engine.scheduler import Engine
+from agent_factory_3_b200.engine.server import build_app
+from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
+
+
+def tiny_model(dev="cpu", lora=None, dtype=torch.float32):
+    cfg = GptOssConfig.tiny()
+    m = GptOssForCausalLM(cfg, lora=lora, device=dev, dtype=dtype).init_random(0)
+    m.eval()
+    return m
+
+
+def greedy_reference(model, prompt, n):
+    ids = list(prompt)
+    out = []
+    for _ in range(n):
+        t = torch.tensor(ids)
+        with torch.no_grad():
+            h = model.forward_hidden(t, torch.arange(len(ids)), torch.tensor([0, len(ids)], dtype=torch.int32))
+            nxt = int(model.logits(h[-1:]).argmax(-1))
+        ids.append(nxt)
+        out.append(nxt)
+    return out
+
+
+def test_kv_cache_prefix_and_eviction():
+    kv = PagedKVCache(2, 6, 4, 2, 16, 2, "cpu", torch.float32)
+    toks = list(range(12))
+    pages, _ = kv.match_prefix(toks, "s")
+    assert pages == []
+    p = kv.allocate(3)
+    prev = b""
+    for i, pg in enumerate(p):
+        prev = kv.chain(prev, toks[i * 4:(i + 1) * 4], "s")
+        kv.register(pg, prev)
+    kv.release(p)
+    got, _ = kv.match_prefix(toks + [99], "s")
+    assert got == p
+    assert kv.match_prefix(toks, "other-salt")[0] == []
+    kv.release(got)
+    kv.allocate(6)   # evicts the cached pages
+    assert kv.match_prefix(toks, "s")[0] == []
+
+
+async def _client(engine):
+    client = TestClient(TestServer(build_app(engine)))
+    await client.start_server()
+    return client
+
+
+def test_engine_greedy_matches_recompute_and_routing():
+    model = tiny_model()
+    eng = Engine(model, num_pages=64, page_size=16, max_prefill_tokens=64).start()
+    prompt = list(range(5, 45))
+
+    async def run():
+        c = await _client(eng)
+        try:
+            body = {"input_ids": prompt, "sampling_params": {"max_new_tokens": 6, "temperature": 0.0},
+                    "return_logprob": True, "return_routed_experts": True, "return_entropy": True}
+            r = await (await c.post("/generate", json=body)).json()
+            r2 = await (await c.post("/generate", json=body)).json()
+            loads = await (await c.get("/v1/loads")).json()
+            return r, r2, loads
+        finally:
+            await c.close()
+
+    try:
+        r, r2, loads = asyncio.run(run())
+    finally:
+        eng.stop()
+    ref = greedy_reference(model, prompt, 6)
+    assert r["output_ids"] == ref
+    meta = r["meta_info"]
+    assert meta["finish_reason"]["type"] == "length" and meta["completion_tokens"] == 6
+    assert len(meta["output_token_logprobs"]) == 6 and len(meta["output_token_entropy"]) == 6
+    rt = np.frombuffer(base64.b64decode(meta["routed_experts"]), dtype=np.int32)
+    assert rt.size == (len(prompt) + 6 - 1) * 2 * 2
+    # the second identical request hits the prefix cache and decodes the same tokens
+    assert r2["output_ids"] == ref and r2["meta_info"]["cached_tokens"] >= 32
+    rt2 = np.frombuffer(base64.b64decode(r2["meta_info"]["routed_experts"]), dtype=np.int32)
+    assert np.array_equal(rt, rt2)
+    assert "num_running_reqs" in loads["loads"][0]
+
+
+def test_pause_abort_continue_and_weight_version():
+    model = tiny_model()
+    eng = Engine(model, num_pages=64, page_size=16).start()
+
+    async def run():
+        c = await _client(eng)
+        try:
+            body = {"input_ids": list(range(10, 30)),
+                    "sampling_params": {"max_new_tokens": 400, "temperature": 1.0}}
+            task = asyncio.create_task((await c.post("/generate", json=body)).json()) if False else None
+            fut = asyncio.ensure_future(c.post("/generate", json=body))
+            await asyncio.sleep(0.3)
+            await c.post("/pause_generation", json={"mode": "abort"})
+            r = await (await fut).json()
+            # a request sent while paused waits for continue
+            await c.post("/update_weight_version", json={"new_version": "7"})
+            fut2 = asyncio.ensure_future(c.post("/generate", json={
+                "input_ids": [1, 2, 3], "sampling_params": {"max_new_tokens": 2}}))
+            await asyncio.sleep(0.2)
+            assert not fut2.done()
+            await c.post("/continue_generation", json={})
+            r2 = await (await fut2).json()
+            return r, r2
+        finally:
+            await c.close()
+
+    try:
+        r, r2 = asyncio.run(run())
+    finally:
+        eng.stop()
+    assert r["meta_info"]["finish_reason"]["type"] == "abort"
+    assert len(r["output_ids"]) < 400
+    assert r2["meta_info"]["weight_version"] == "7"
+
+
+def test_lora_hot_swap_and_merged_reload(tmp_path):
+    from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
+    from agent_factory_3_b200.trainer.training_config import TrainingConfig
+    lora = LoraConfig(r=4, lora_alpha=8, target_modules=["q_proj", "v_proj", "o_proj"])
+    tcfg = TrainingConfig(model_id="tiny", lora_r=4, lora_alpha=8,
+                          lora_target_modules=["q_proj", "v_proj", "o_proj"], random_init_seed=0)
+    tr = ModelTrainer(tcfg, device="cpu")
+    with torch.no_grad():
+        for p in tr.model.parameters():
+            if p.requires_grad:
+                p.normal_(0, 0.3)
+    tr.save_model(str(tmp_path / "adapter"))
+    tr.save_merged_weights(str(tmp_path / "merged"))
+    served = GptOssForCausalLM(GptOssConfig.tiny(), lora=lora, dtype=torch.float32)
+    served.load_state_dict({k: v for k, v in tr.model.state_dict().items() if "lora" not in k}, strict=False)
+    served.eval()
+    eng = Engine(served, num_pages=64, page_size=16).start()
+    prompt = list(range(3, 30))
+
+    async def run():
+        c = await _client(eng)
+        try:
+            body = {"input_ids": prompt, "sampling_params": {"max_new_tokens": 5, "temperature": 0.0}}
+            base = await (await c.post("/generate", json=body)).json()
+            r = await c.post("/load_lora_adapter", json={"lora_name": "policy",
+                                                          "lora_path": str(tmp_path / "adapter")})
+            assert r.status == 200
+            adapted = await (await c.post("/generate", json=dict(body, lora_path="policy"))).json()
+            await c.post("/update_weights_from_disk", json={"model_path": str(tmp_path / "merged"),
+                                                            "flush_cache": True, "weight_version": "m1"})
+            merged = await (await c.post("/generate", json=body)).json()
+            bad = await c.post("/unload_lora_adapter", json={"lora_name": "missing"})
+            return base, adapted, merged, bad.status
+        finally:
+            await c.close()
+
+    try:
+        base, adapted, merged, bad = asyncio.run(run())
+    finally:
+        eng.stop()
+    ref_adapted = greedy_reference(tr.model, prompt, 5)
+    assert adapted["output_ids"] == ref_adapted
+    assert merged["output_ids"] == ref_adapted      # LoRA folded into the base weights
+    assert merged["meta_info"]["weight_version"] == "m1"
+    assert bad == 400
