@@ -24,6 +24,7 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
   AF3_CHECK(M >= 0 && N > 0 && K > 0, "bad GEMM shape");
   AF3_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "GEMM dims must fit int32");
   const c10::cuda::CUDAGuard guard(a.device());
+  if (M == 0) return;  // nothing to compute (and TMA descriptors cannot describe empty tensors)
   GemmOperands o;
   o.a = a.data_ptr();
   o.a_mn = a_mn;

@@ -157,6 +157,9 @@ class ModelRunner:
         self.kv.routing.view(-1, cfg.num_hidden_layers, cfg.num_experts_per_tok)[slots_t.long()] = routing
         last = torch.tensor([r[1] - 1 for r, it in zip(rows, items) if it.want_logits],
                             device=dev, dtype=torch.long)
+        if last.numel() == 0:  # only partial prefill chunks this step
+            return StepOutput(logits=torch.empty(0, cfg.vocab_size, device=dev), routing=routing,
+                              item_rows=rows)
         hl = rmsnorm(x.index_select(0, last), self.model.norm, cfg.rms_norm_eps)
         logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
         return StepOutput(logits=logits, routing=routing, item_rows=rows)
