@@ -57,6 +57,10 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
     async def generate(request: web.Request):
         body = await request.json()
         req = _request_from_json(body)
+        vocab = engine.model.cfg.vocab_size
+        if min(req.input_ids) < 0 or max(req.input_ids) >= vocab:
+            # never let an out-of-range id reach the embedding gather on the device
+            return web.json_response({"error": f"input_ids must lie in [0, {vocab})"}, status=400)
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         req.on_output = lambda out: loop.call_soon_threadsafe(q.put_nowait, out)
