@@ -4,6 +4,7 @@
     python -m agent_factory_3_b200.benchmarks.kernels --op attn_bwd --seqlens 8192
     python -m agent_factory_3_b200.benchmarks.kernels --op gemm --m 16384 --n 5760 --k 2880
     python -m agent_factory_3_b200.benchmarks.kernels --op moe --tokens 32768
+    python -m agent_factory_3_b200.benchmarks.kernels --op dequant --experts 128
 
 Each run prints one JSON line with the time per call, the achieved TFLOP/s (or GB/s) and the
 fraction of the measured peak in MEASURED_PEAKS.json (when present).
@@ -116,9 +117,20 @@ def bench_moe(args):
     return {"flops": 2 * T * K * 2 * I * H, "ms": ms}
 
 
+def bench_dequant(args):
+    """MXFP4 -> bf16 of one gpt-oss-120b gate_up expert stack [E, 5760, 2880]."""
+    from ..ops._ext import ext
+    E, N, K = args.experts, 5760, 2880
+    blocks = torch.randint(0, 256, (E, N, K // 32, 16), dtype=torch.uint8, device="cuda")
+    scales = torch.randint(112, 130, (E, N, K // 32), dtype=torch.uint8, device="cuda")
+    out = torch.empty(E, N, K, dtype=torch.bfloat16, device="cuda")
+    ms = _time(lambda: ext().mxfp4_dequant(blocks, scales, out), args.iters)
+    return {"bytes": blocks.numel() + scales.numel() + out.numel() * 2, "ms": ms}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe"])
+    ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe", "dequant"])
     ap.add_argument("--seqlens", default="8192")
     ap.add_argument("--hq", type=int, default=64)
     ap.add_argument("--hkv", type=int, default=8)
@@ -127,6 +139,7 @@ def main():
     ap.add_argument("--n", type=int, default=5760)
     ap.add_argument("--k", type=int, default=2880)
     ap.add_argument("--tokens", type=int, default=32768)
+    ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args()
     if args.op == "attn_fwd":
@@ -135,9 +148,16 @@ def main():
         r = bench_attention(args, True)
     elif args.op == "gemm":
         r = bench_gemm(args)
+    elif args.op == "dequant":
+        r = bench_dequant(args)
     else:
         r = bench_moe(args)
-    peak_tf, _, kind = _peaks()
+    peak_tf, peak_bw, kind = _peaks()
+    if "bytes" in r:
+        gbs = r["bytes"] / (r["ms"] / 1e3) / 1e9
+        print(json.dumps({"op": args.op, "ms": round(r["ms"], 4), "gb_per_s": round(gbs, 1),
+                          f"frac_of_{kind}_hbm": round(gbs / peak_bw, 3), "args": vars(args)}))
+        return
     tf = r["flops"] / (r["ms"] / 1e3) / 1e12
     print(json.dumps({"op": args.op, "ms": round(r["ms"], 4), "tflops": round(tf, 1),
                       f"frac_of_{kind}_bf16_peak": round(tf / peak_tf, 3), "args": vars(args)}))

@@ -16,43 +16,47 @@
 namespace af3 {
 
 // ------------------------------------ MXFP4 ------------------------------------------
-__constant__ float kFp4Lut[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  4.0f,  6.0f,
-                                  -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
-
-__device__ __forceinline__ float e8m0_to_float(uint32_t s) {
-  // 2^(s-127) exactly; s == 0 is the fp32 subnormal 2^-127, s == 255 maps to +inf
-  if (s == 0) return __int_as_float(0x00400000);
-  if (s == 255) return __int_as_float(0x7f800000);
-  return __int_as_float(s << 23);
+// e2m1 -> bf16 without a table.  For a nibble s|e1 e0|m, placing the three magnitude bits at
+// bf16 bits 8..6 (exponent bits 1..0 and the top mantissa bit) and the sign at bit 15 gives
+// the bf16 whose value is exactly e2m1(nibble) * 2^-126: e = 0 lands in the bf16 subnormal
+// range (m * 2^-127) and e > 0 in the normal range (2^(e-127) * (1 + m/2)).  Two exact
+// power-of-two multiplies (by 2^126 and by the block scale 2^(s-127)) then give the value.
+// Four packed bytes (eight values, low nibble first) -> four bf16x2 words.
+__device__ __forceinline__ uint32_t e2m1x2_to_bf16x2_unscaled(uint32_t byte) {
+  const uint32_t t = byte * 0x1001u;  // low nibble at bits 0..3, high nibble at bits 16..19
+  return ((t << 6) & 0x01C001C0u) | ((t << 12) & 0x80008000u);
 }
 
-// One thread per 32-element block: 16 packed bytes + 1 scale -> 32 bf16 (64 bytes).
-__global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks,
-                                     const uint8_t* __restrict__ scales,
-                                     __nv_bfloat16* __restrict__ out, int64_t n_blocks) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_blocks;
+// bf16 bits of 2^(s-127) (e8m0 scale): s = 0 is the subnormal 2^-127, s = 255 is +inf.
+__device__ __forceinline__ uint32_t e8m0_to_bf16_bits(uint32_t s) {
+  return s ? (s << 7) : 0x40u;
+}
+
+__device__ __forceinline__ uint4 e2m1x8_to_bf16x8(uint32_t w, uint32_t scale_bits) {
+  const uint32_t k2p126 = 0x7E807E80u;  // bf16x2 (2^126, 2^126)
+  const uint32_t sc2 = scale_bits | (scale_bits << 16);
+  const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&k2p126);
+  const __nv_bfloat162 sc = *reinterpret_cast<const __nv_bfloat162*>(&sc2);
+  uint32_t r[4];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    uint32_t x = e2m1x2_to_bf16x2_unscaled((w >> (8 * b)) & 0xFFu);
+    __nv_bfloat162 v = __hmul2(__hmul2(*reinterpret_cast<__nv_bfloat162*>(&x), c), sc);
+    r[b] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// One thread per 4 packed bytes (8 values, 16 output bytes): loads and stores of a warp are
+// contiguous (128 B in, 512 B out); the 4 threads of one 32-element block share its scale.
+__global__ void mxfp4_dequant_kernel(const uint32_t* __restrict__ words,
+                                     const uint8_t* __restrict__ scales, uint4* __restrict__ out,
+                                     int64_t n_words) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_words;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 w = *reinterpret_cast<const uint4*>(blocks + i * 16);
-    const float sc = e8m0_to_float(scales[i]);
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    uint4* dst = reinterpret_cast<uint4*>(out + i * 32);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t x = words[q];
-      float v[8];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (x >> (8 * b)) & 0xff;
-        v[2 * b] = kFp4Lut[byte & 0xf] * sc;
-        v[2 * b + 1] = kFp4Lut[byte >> 4] * sc;
-      }
-      uint4 o;
-      o.x = pack_bf16x2(v[0], v[1]);
-      o.y = pack_bf16x2(v[2], v[3]);
-      o.z = pack_bf16x2(v[4], v[5]);
-      o.w = pack_bf16x2(v[6], v[7]);
-      dst[q] = o;
-    }
+    const uint32_t w = __ldg(words + i);
+    const uint32_t s = __ldg(scales + (i >> 2));
+    out[i] = e2m1x8_to_bf16x8(w, e8m0_to_bf16_bits(s));
   }
 }
 
@@ -65,13 +69,17 @@ void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out
   const int64_t n = scales.numel();
   AF3_CHECK(blocks.numel() == n * 16 && out.numel() == n * 32, "mxfp4 shape mismatch");
   AF3_CHECK(out.scalar_type() == torch::kBFloat16, "out must be bf16");
+  AF3_CHECK(reinterpret_cast<uintptr_t>(blocks.data_ptr()) % 4 == 0 &&
+                reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+            "mxfp4_dequant needs 4-byte aligned blocks and 16-byte aligned out");
   const c10::cuda::CUDAGuard guard(blocks.device());
   if (n == 0) return;
   const int threads = 256;
-  const int64_t grid = std::min<int64_t>((n + threads - 1) / threads, (int64_t)num_sms() * 16);
+  const int64_t n_words = n * 4;
+  const int64_t grid = std::min<int64_t>((n_words + threads - 1) / threads, (int64_t)num_sms() * 32);
   mxfp4_dequant_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      blocks.data_ptr<uint8_t>(), scales.data_ptr<uint8_t>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n);
+      reinterpret_cast<const uint32_t*>(blocks.data_ptr<uint8_t>()), scales.data_ptr<uint8_t>(),
+      reinterpret_cast<uint4*>(out.data_ptr()), n_words);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -45,7 +45,23 @@ def parse_args():
     ap.add_argument("--lora-alpha", type=int, default=64)
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--trace", default=None,
+                    help="after the timed steps, run one more step under torch.profiler and write "
+                         "its per-kernel device-time table (text) to this path")
     return ap.parse_args()
+
+
+def write_trace(step, path: str) -> None:
+    """One untimed step under torch.profiler: kernel table sorted by device time."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    table = prof.key_averages().table(sort_by="self_device_time_total", row_limit=60,
+                                      max_name_column_width=90)
+    with open(path, "w") as f:
+        f.write(table)
 
 
 def reference_unavailable(args) -> None:
@@ -277,6 +293,8 @@ def main():
             "loss": losses[-1],
         }
         print(json.dumps(out), flush=True)
+    if args.trace:
+        write_trace(step, args.trace if world == 1 else f"{args.trace}.rank{rank}")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

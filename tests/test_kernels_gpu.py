@@ -16,6 +16,16 @@ def test_mxfp4_dequant_bit_exact(dev):
     assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
 
 
+def test_mxfp4_dequant_exhaustive(dev):
+    """Every packed byte under every finite e8m0 scale (0 = 2^-127 .. 254), bit for bit."""
+    s = torch.arange(255, dtype=torch.uint8)
+    blocks = torch.arange(256, dtype=torch.int64).to(torch.uint8).view(1, 16, 16).repeat(255, 1, 1)
+    scales = s.view(255, 1).repeat(1, 16)
+    ref = mxfp4.dequantize_reference(blocks, scales)
+    out = mxfp4.dequantize(blocks.to(dev), scales.to(dev))
+    assert torch.equal(out.cpu().view(torch.int16), ref.view(torch.int16))
+
+
 @pytest.mark.parametrize("replay", [False, True])
 def test_route_and_group(dev, replay):
     torch.manual_seed(1)
