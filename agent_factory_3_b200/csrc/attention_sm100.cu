@@ -1,52 +1,54 @@
-// Flash attention for gpt-oss on sm_100a: causal GQA over packed variable-length sequences,
-// optional sliding window, learned per-head sinks, head_dim 64.
+// Flash attention forward for gpt-oss on sm_100a: causal GQA over packed variable-length
+// sequences, optional sliding window, learned per-head sinks, head_dim 64.
 //
-// Forward, one CTA per (128-query tile, q head):
-//   warp 0   TMA: Q tile once, then K_j (K-major) and V_j (MN-major, two 64-key boxes)
-//            into a 3-stage ring
-//   warp 1   tcgen05 issuer: S_j = Q K_j^T into TMEM S[j%2] (M=128, N=128, K=64), and one
-//            block later O_j = P_j V_j into TMEM O[j%2] (M=128, N=64, K=128)
-//   warps 4-7 softmax: thread t owns query row t; reads S_j with tcgen05.ld, applies the
-//            causal / window / sequence masks, online max and row sum in the log2 domain,
-//            writes P_j (bf16) into 128B-swizzled shared memory for the PV MMA, and
-//            accumulates O = O * 2^(m_old - m_new) + O_j in registers.
+// One CTA per (q head, span of up to 256 query rows).  The span is two 128-row tiles A and B
+// that share every K/V block loaded by TMA; each tile has its own softmax warpgroup, so the
+// tensor core works on one tile while the other tile's softmax runs.
+//   warp 0      TMA: Q_A, Q_B once, then K_j (K-major) and V_j (MN-major, two 64-key boxes)
+//               into a 3-stage ring
+//   warp 1      tcgen05 issuer, in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1):
+//               S_X = Q_X K_j^T (M=128, N=128, K=64) into TMEM S[X]; O_X += P_X V_j (M=128,
+//               N=64, K=128) accumulated in TMEM O[X] across all key blocks, and the row sums
+//               l_X += P_X 1 (M=128, N=16, K=128 against a constant tile of ones) beside it
+//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: thread t owns query row t;
+//               reads S with tcgen05.ld, applies the causal / window / sequence masks, keeps a
+//               reference max m (log2 domain) that only moves when a block's max exceeds it by
+//               more than 2^8 (then O in TMEM and the row sum are rescaled once), writes
+//               P = 2^(s*scale*log2e - m) as bf16 into 128B-swizzled shared memory
 //   The sink logit joins the denominator at the end: l += 2^(sink*log2e - m).
 //   Outputs: O (bf16) and the natural-log LSE per (head, query), sink included.
 //
-// Backward, one CTA per (128-key tile, q head): recomputes S^T = K Q^T and P^T, computes
-// dP^T = V dO^T, dS^T = P^T (dP^T - D), accumulates dV += P^T dO and dK += dS^T Q in TMEM,
-// and reduces dQ += dS K into an fp32 buffer with bulk tensor reduce-add.  dK/dV of the
-// q heads sharing a kv head are summed with fp32 atomics.  d(sink_h) = -sum_i p_sink(i) D_i.
-//
 // Reference semantics: HF transformers eager_attention_forward for gpt-oss (sinks appended to
-// the logits, softmax, sink column dropped); sliding window: key j visible from query i iff
-// i - j < window.
+// the logits, softmax, sink column dropped; models/gpt_oss in transformers); sliding window:
+// key j visible from query i iff i - j < window.
 #include "common.h"
 #include "host_utils.h"
 #include "sm100.cuh"
 
 namespace af3 {
 
-constexpr int kAttnThreads = 256;
+constexpr int kFwdThreads = 384;
 constexpr int kHD = 64;  // head dim
 constexpr int kBQ = 128;
 constexpr int kBKV = 128;
 constexpr int kKVStages = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleLog2 = 8.0f;  // reference max moves only when exceeded by 2^8
 
 struct AttnFwdSmem {
   // all tiles 1024-aligned
-  static constexpr int Q = 0;                                  // 16 KB
-  static constexpr int K = Q + kBQ * kHD * 2;                  // 3 x 16 KB
+  static constexpr int Q = 0;                                  // 2 x 16 KB (A, B)
+  static constexpr int K = Q + 2 * kBQ * kHD * 2;              // 3 x 16 KB
   static constexpr int V = K + kKVStages * kBKV * kHD * 2;     // 3 x 16 KB
-  static constexpr int P = V + kKVStages * kBKV * kHD * 2;     // 2 x 32 KB
-  static constexpr int BAR = P + 2 * kBQ * kBKV * 2;
+  static constexpr int P = V + kKVStages * kBKV * kHD * 2;     // 2 x 32 KB (A, B)
+  static constexpr int ONES = P + 2 * kBQ * kBKV * 2;          // 4 KB: bf16 ones [16 x 128]
+  static constexpr int BAR = ONES + 16 * kBKV * 2;
   static constexpr int TOTAL = BAR + 1024;
 };
 
 struct AttnParams {
-  const int* tiles;  // [n, 3] (seq_start, q_start, q_end)
+  const int* tiles;  // [n, 3] (seq_start, q_start, q_end), q_end - q_start <= 256
   const float* sinks;
   __nv_bfloat16* out;
   int64_t ld_out;
@@ -62,7 +64,79 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
+// Key-block range of one 128-row query tile inside the CTA's span.
+struct FwdTile {
+  int q0, q1;    // query rows [q0, q1); empty when q1 <= q0
+  int jlo, jhi;  // key blocks [jlo, jhi) relative to the span's first key
+};
+
+__device__ __forceinline__ FwdTile fwd_tile(int q0, int q1, int seq0, int kv_lo, int window) {
+  FwdTile t{q0, q1, 0, 0};
+  if (q1 > q0) {
+    const int lo = window > 0 ? max(seq0, q0 - window + 1) : seq0;
+    t.jlo = (lo - kv_lo) / kBKV;
+    t.jhi = (q1 - 1 - kv_lo) / kBKV + 1;
+  }
+  return t;
+}
+
+// MMA-issuer state of one tile (kept in registers: the tile index is a template argument).
+struct FwdIssue {
+  int jlo, jhi;  // key blocks of the tile
+  int n_s, n_pv; // S / PV blocks issued so far
+};
+
+template <int X>
+__device__ __forceinline__ bool fwd_issue_s(FwdIssue& t, int j, uint32_t tmem, uint32_t sq,
+                                            uint32_t sk0, uint64_t* s_empty, uint64_t* s_full,
+                                            int* err, volatile int* abort_flag) {
+  if (j < t.jlo || j >= t.jhi) return true;
+  if (!mbar_wait(&s_empty[X], (t.n_s & 1) ^ 1, err, abort_flag)) return false;
+  tc_fence_after();
+  constexpr uint32_t idesc_s = make_idesc_bf16(kBQ, kBKV, false, false);
+  const uint32_t q = sq + X * kBQ * kHD * 2;
+  const uint32_t k = sk0 + (j % kKVStages) * kBKV * kHD * 2;
+#pragma unroll
+  for (int kk = 0; kk < kHD / 16; ++kk) {
+    umma_f16(tmem + X * kBKV, make_smem_desc(q + kk * 32, 16, 1024, kLayoutSW128),
+             make_smem_desc(k + kk * 32, 16, 1024, kLayoutSW128), idesc_s, kk > 0);
+  }
+  umma_commit(&s_full[X]);
+  ++t.n_s;
+  return true;
+}
+
+template <int X>
+__device__ __forceinline__ bool fwd_issue_pv(FwdIssue& t, int j, uint32_t tmem, uint32_t sp0,
+                                             uint32_t sv0, uint64_t* p_full, uint64_t* o_done,
+                                             int* err, volatile int* abort_flag) {
+  if (j < t.jlo || j >= t.jhi) return true;
+  if (!mbar_wait(&p_full[X], t.n_pv & 1, err, abort_flag)) return false;
+  tc_fence_after();
+  constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, kHD, false, true);
+  constexpr uint32_t idesc_l = make_idesc_bf16(kBQ, 16, false, false);
+  const uint32_t pp = sp0 + X * kBQ * kBKV * 2;
+  const uint32_t ones = sp0 + 2 * kBQ * kBKV * 2;
+  const uint32_t v = sv0 + (j % kKVStages) * kBKV * kHD * 2;
+  const uint32_t first = t.n_pv > 0 ? 1u : 0u;
+#pragma unroll
+  for (int kk = 0; kk < kBKV / 16; ++kk) {
+    const uint64_t ad = make_smem_desc(pp + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
+    const uint64_t bd = make_smem_desc(v + (kk / 4) * 8192 + (kk % 4) * 2048, 8192, 1024, kLayoutSW128);
+    umma_f16(tmem + 256 + X * kHD, ad, bd, idesc_o, kk > 0 ? 1u : first);
+  }
+#pragma unroll
+  for (int kk = 0; kk < kBKV / 16; ++kk) {  // row sums of P: P x ones[16 x 128]^T
+    const uint64_t ad = make_smem_desc(pp + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
+    const uint64_t bd = make_smem_desc(ones + (kk / 4) * 2048 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
+    umma_f16(tmem + 384 + X * 16, ad, bd, idesc_l, kk > 0 ? 1u : first);
+  }
+  umma_commit(&o_done[X]);
+  ++t.n_pv;
+  return true;
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qk,
                     const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -72,25 +146,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;    // [3]
   uint64_t* kv_empty = bars + 4;   // [3]
-  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* s_full = bars + 7;     // [2] per tile
   uint64_t* s_empty = bars + 9;    // [2]
   uint64_t* p_full = bars + 11;    // [2]
-  uint64_t* o_full = bars + 13;    // [2]
-  uint64_t* o_empty = bars + 15;   // [2]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* o_done = bars + 13;    // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int h = blockIdx.x;
-  const int tile = blockIdx.y;
-  const int seq0 = p.tiles[tile * 3 + 0];
-  const int q0 = p.tiles[tile * 3 + 1];
-  const int q1 = p.tiles[tile * 3 + 2];
-  if (q1 <= q0) return;
+  const int span = blockIdx.y;
+  const int seq0 = p.tiles[span * 3 + 0];
+  const int qs0 = p.tiles[span * 3 + 1];
+  const int qs1 = p.tiles[span * 3 + 2];
+  if (qs1 <= qs0) return;
   const int kvh = h / (p.hq / p.hkv);
-  int kv_lo = seq0;
-  if (p.window > 0) kv_lo = max(seq0, q0 - p.window + 1);
-  const int nb = (q1 - kv_lo + kBKV - 1) / kBKV;
+  const int kv_lo = p.window > 0 ? max(seq0, qs0 - p.window + 1) : seq0;
+  const int nb = (qs1 - kv_lo + kBKV - 1) / kBKV;
+  const FwdTile tl[2] = {fwd_tile(qs0, min(qs1, qs0 + kBQ), seq0, kv_lo, p.window),
+                         fwd_tile(qs0 + kBQ, qs1, seq0, kv_lo, p.window)};
+  const bool has_b = tl[1].q1 > tl[1].q0;
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_qk);
@@ -100,12 +175,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
-      mbar_init(&p_full[b], 128);
-      mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&s_empty[x], 128);
+      mbar_init(&p_full[x], 128);
+      mbar_init(&o_done[x], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -114,195 +188,192 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
+  for (int i = threadIdx.x; i < 16 * kBKV * 2 / 16; i += blockDim.x)  // bf16 1.0 = 0x3F80
+    st_shared_v4(smem_u32(smem + AttnFwdSmem::ONES) + i * 16, 0x3F803F80u, 0x3F803F80u,
+                 0x3F803F80u, 0x3F803F80u);
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  // TMEM columns: S[0] 0..127, S[1] 128..255, O[0] 256..319, O[1] 320..383
+  // TMEM columns: S[A] 0..127, S[B] 128..255, O[A] 256..319, O[B] 320..383,
+  //               l[A] 384..399, l[B] 400..415 (16 equal columns each)
 
-  if (warp == 0) {
-    if (elect_one_sync()) {
-      mbar_arrive_expect_tx(q_full, kBQ * kHD * 2);
-      tma_load_2d(smem + AttnFwdSmem::Q, &tma_qk, q_full, h * kHD, q0);
-      for (int j = 0; j < nb; ++j) {
-        const int s = j % kKVStages;
-        if (!mbar_wait(&kv_empty[s], ((j / kKVStages) & 1) ^ 1, p.err, abort_flag)) break;
-        const int k0 = kv_lo + j * kBKV;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kBKV * kHD * 2);
-        tma_load_2d(smem + AttnFwdSmem::K + s * kBKV * kHD * 2, &tma_qk, &kv_full[s],
-                    (p.hq + kvh) * kHD, k0);
-        uint8_t* vb = smem + AttnFwdSmem::V + s * kBKV * kHD * 2;
-        tma_load_2d(vb, &tma_v, &kv_full[s], (p.hq + p.hkv + kvh) * kHD, k0);
-        tma_load_2d(vb + 8192, &tma_v, &kv_full[s], (p.hq + p.hkv + kvh) * kHD, k0 + 64);
-      }
-    }
-  } else if (warp == 1) {
-    if (elect_one_sync()) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(kBQ, kBKV, false, false);
-      constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, kHD, false, true);
-      const uint32_t sq = smem_u32(smem + AttnFwdSmem::Q);
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag);
-      for (int j = 0; ok && j <= nb; ++j) {
-        if (j < nb) {
+  // register split (launch: 384 x 168): control warps 128 x 96 + softmax 256 x 200 = 63488 <= 64512
+  if (warp < 4) {
+    setmaxnreg_dec<96>();
+    if (warp == 0) {
+      if (elect_one_sync()) {
+        mbar_arrive_expect_tx(q_full, (has_b ? 2 : 1) * kBQ * kHD * 2);
+        tma_load_2d(smem + AttnFwdSmem::Q, &tma_qk, q_full, h * kHD, qs0);
+        if (has_b) tma_load_2d(smem + AttnFwdSmem::Q + kBQ * kHD * 2, &tma_qk, q_full, h * kHD, qs0 + kBQ);
+        for (int j = 0; j < nb; ++j) {
           const int s = j % kKVStages;
-          if (!mbar_wait(&kv_full[s], (j / kKVStages) & 1, p.err, abort_flag)) break;
-          if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t sk = smem_u32(smem + AttnFwdSmem::K + s * kBKV * kHD * 2);
-#pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            umma_f16(tmem + (j & 1) * kBKV, make_smem_desc(sq + kk * 32, 16, 1024, kLayoutSW128),
-                     make_smem_desc(sk + kk * 32, 16, 1024, kLayoutSW128), idesc_s, kk > 0);
-          }
-          umma_commit(&s_full[j & 1]);
+          if (!mbar_wait(&kv_empty[s], ((j / kKVStages) & 1) ^ 1, p.err, abort_flag)) break;
+          const int k0 = kv_lo + j * kBKV;
+          mbar_arrive_expect_tx(&kv_full[s], 2 * kBKV * kHD * 2);
+          tma_load_2d(smem + AttnFwdSmem::K + s * kBKV * kHD * 2, &tma_qk, &kv_full[s],
+                      (p.hq + kvh) * kHD, k0);
+          uint8_t* vb = smem + AttnFwdSmem::V + s * kBKV * kHD * 2;
+          tma_load_2d(vb, &tma_v, &kv_full[s], (p.hq + p.hkv + kvh) * kHD, k0);
+          tma_load_2d(vb + 8192, &tma_v, &kv_full[s], (p.hq + p.hkv + kvh) * kHD, k0 + 64);
         }
-        if (j >= 1) {
-          const int i = j - 1;
-          const int s = i % kKVStages;
-          if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.err, abort_flag)) break;
-          if (!mbar_wait(&o_empty[i & 1], ((i >> 1) & 1) ^ 1, p.err, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t sp = smem_u32(smem + AttnFwdSmem::P + (i & 1) * kBQ * kBKV * 2);
-          const uint32_t sv = smem_u32(smem + AttnFwdSmem::V + s * kBKV * kHD * 2);
-#pragma unroll
-          for (int kk = 0; kk < kBKV / 16; ++kk) {
-            const uint64_t ad =
-                make_smem_desc(sp + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
-            const uint64_t bd =
-                make_smem_desc(sv + (kk / 4) * 8192 + (kk % 4) * 2048, 8192, 1024, kLayoutSW128);
-            umma_f16(tmem + 256 + (i & 1) * kHD, ad, bd, idesc_o, kk > 0);
+      }
+    } else if (warp == 1) {
+      if (elect_one_sync()) {
+        const uint32_t sq = smem_u32(smem + AttnFwdSmem::Q);
+        const uint32_t sk0 = smem_u32(smem + AttnFwdSmem::K);
+        const uint32_t sv0 = smem_u32(smem + AttnFwdSmem::V);
+        const uint32_t sp0 = smem_u32(smem + AttnFwdSmem::P);
+        FwdIssue a{tl[0].jlo, tl[0].jhi, 0, 0}, b{tl[1].jlo, tl[1].jhi, 0, 0};
+        bool ok = mbar_wait(q_full, 0, p.err, abort_flag) &&
+                  mbar_wait(&kv_full[0], 0, p.err, abort_flag);
+        ok = ok && fwd_issue_s<0>(a, 0, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag) &&
+             fwd_issue_s<1>(b, 0, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
+        for (int j = 0; ok && j < nb; ++j) {
+          ok = fwd_issue_pv<0>(a, j, tmem, sp0, sv0, p_full, o_done, p.err, abort_flag);
+          if (ok && j + 1 < nb) {
+            ok = mbar_wait(&kv_full[(j + 1) % kKVStages], ((j + 1) / kKVStages) & 1, p.err,
+                           abort_flag) &&
+                 fwd_issue_s<0>(a, j + 1, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
           }
-          umma_commit(&o_full[i & 1]);
-          umma_commit(&kv_empty[s]);
+          ok = ok && fwd_issue_pv<1>(b, j, tmem, sp0, sv0, p_full, o_done, p.err, abort_flag);
+          if (ok && j + 1 < nb)
+            ok = fwd_issue_s<1>(b, j + 1, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
+          umma_commit(&kv_empty[j % kKVStages]);
         }
       }
     }
-  } else if (warp >= 4) {
+  } else {
+    setmaxnreg_inc<200>();
+    const int x = (warp - 4) >> 2;  // tile owned by this warpgroup
+    const FwdTile t = x ? tl[1] : tl[0];
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const int qi = q0 + row;
+    const int qi = t.q0 + row;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    float o_acc[kHD];
-#pragma unroll
-    for (int d = 0; d < kHD; ++d) o_acc[d] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, m_acc = -INFINITY;
-    float m_hist[2] = {-INFINITY, -INFINITY};
-    uint8_t* pbase = smem + AttnFwdSmem::P;
+    const uint32_t s_addr = tmem + lane_base + x * kBKV;
+    const uint32_t o_addr = tmem + lane_base + 256 + x * kHD;
+    const uint32_t l_addr = tmem + lane_base + 384 + x * 16;
+    const uint32_t prow = smem_u32(smem + AttnFwdSmem::P + x * kBQ * kBKV * 2 + row * 128);
+    float m_ref = -INFINITY;
+    int c = 0;
     bool ok = true;
-    for (int j = 0; j <= nb && ok; ++j) {
-      if (j < nb) {
-        if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        float sv[kBKV];
-        {
-          uint32_t r0[32], r1[32], r2[32], r3[32];
-          const uint32_t ta = tmem + lane_base + (j & 1) * kBKV;
-          tmem_ld_32x32b_x32(ta, r0);
-          tmem_ld_32x32b_x32(ta + 32, r1);
-          tmem_ld_32x32b_x32(ta + 64, r2);
-          tmem_ld_32x32b_x32(ta + 96, r3);
-          tmem_ld_wait();
-          // raw scores; the softmax scale is applied inside the exp2 argument (one FFMA)
+    for (int j = t.jlo; j < t.jhi; ++j, ++c) {
+      if (!mbar_wait(&s_full[x], c & 1, p.err, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float sv[kBKV];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld_32x32b_x32(s_addr, r0);
+        tmem_ld_32x32b_x32(s_addr + 32, r1);
+        tmem_ld_32x32b_x32(s_addr + 64, r2);
+        tmem_ld_32x32b_x32(s_addr + 96, r3);
+        tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            sv[e] = __uint_as_float(r0[e]);
-            sv[32 + e] = __uint_as_float(r1[e]);
-            sv[64 + e] = __uint_as_float(r2[e]);
-            sv[96 + e] = __uint_as_float(r3[e]);
-          }
+        for (int e = 0; e < 32; ++e) {
+          sv[e] = __uint_as_float(r0[e]);
+          sv[32 + e] = __uint_as_float(r1[e]);
+          sv[64 + e] = __uint_as_float(r2[e]);
+          sv[96 + e] = __uint_as_float(r3[e]);
         }
-        tc_fence_before();
-        mbar_arrive(&s_empty[j & 1]);
-        // masks
-        const int k0 = kv_lo + j * kBKV;
-        const bool need_mask = (k0 + kBKV - 1 > q0) || (k0 < seq0) ||
-                               (p.window > 0 && q0 + kBQ - 1 - k0 >= p.window);
-        if (need_mask) {
-#pragma unroll
-          for (int c = 0; c < kBKV; ++c) {
-            const int kj = k0 + c;
-            const bool vis = kj <= qi && kj >= seq0 && (p.window == 0 || qi - kj < p.window);
-            if (!vis) sv[c] = -INFINITY;
-          }
-        }
-        // row max as a tree of independent chains (raw score units)
-        float mxp[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mxp[t] = sv[t];
-#pragma unroll
-        for (int c = 8; c < kBKV; c += 8) {
-#pragma unroll
-          for (int t = 0; t < 8; ++t) mxp[t] = fmaxf(mxp[t], sv[c + t]);
-        }
-        float mraw = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                           fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-        const float mx = fmaxf(m_run, mraw * p.scale_log2);
-        const float m_use = (mx == -INFINITY) ? 0.f : mx;
-        const float alpha = ex2(m_run - m_use);  // m_run = -inf -> 0
-        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        // P_j -> shared memory (bf16, 128B swizzle, two 64-key column blocks)
-        uint8_t* prow = pbase + (j & 1) * kBQ * kBKV * 2 + row * 128;
-#pragma unroll
-        for (int c8 = 0; c8 < kBKV / 8; ++c8) {
-          float pv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            pv[e] = ex2(fmaf(sv[c8 * 8 + e], p.scale_log2, -m_use));
-            rsp[e] += pv[e];
-          }
-          uint4 w;
-          w.x = pack_bf16x2(pv[0], pv[1]);
-          w.y = pack_bf16x2(pv[2], pv[3]);
-          w.z = pack_bf16x2(pv[4], pv[5]);
-          w.w = pack_bf16x2(pv[6], pv[7]);
-          const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
-          *reinterpret_cast<uint4*>(prow + blk * 16384 + ch * 16) = w;
-        }
-        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-        l_run = l_run * alpha + rs;
-        m_run = mx;
-        m_hist[j & 1] = m_use;
-        fence_proxy_async_smem();
-        mbar_arrive(&p_full[j & 1]);
       }
-      if (j >= 1) {
-        const int i = j - 1;
-        if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const float mi = m_hist[i & 1];
-        const float sc = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - mi);
+      tc_fence_before();
+      mbar_arrive(&s_empty[x]);
+      const int k0 = kv_lo + j * kBKV;
+      const bool need_mask = (k0 + kBKV - 1 > t.q0) || (k0 < seq0) ||
+                             (p.window > 0 && t.q0 + kBQ - 1 - k0 >= p.window);
+      if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < kHD / 32; ++c) {
+        for (int cc = 0; cc < kBKV; ++cc) {
+          const int kj = k0 + cc;
+          const bool vis = kj <= qi && kj >= seq0 && (p.window == 0 || qi - kj < p.window);
+          if (!vis) sv[cc] = -INFINITY;
+        }
+      }
+      float mxp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(sv[u], sv[8 + u]);
+#pragma unroll
+      for (int cc = 16; cc < kBKV; cc += 16) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mxp[u] = fmax3(mxp[u], sv[cc + u], sv[cc + 8 + u]);
+      }
+      const float mraw = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]),
+                               fmaxf(mxp[6], mxp[7]));
+      const float cand = mraw * p.scale_log2;
+      const bool resc = cand > m_ref + kRescaleLog2;  // false while both are -inf
+      float alpha = 1.f;
+      if (resc) {
+        alpha = ex2(m_ref - cand);  // m_ref = -inf -> 0
+        m_ref = cand;
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // S(j) was issued after PV(j-1) by the same thread and its commit covers every earlier
+      // MMA, so PV(j-1) is complete here: the P buffer is free and O is stable.
+#pragma unroll
+      for (int c8 = 0; c8 < kBKV / 8; ++c8) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pv[e] = ex2(fmaf(sv[c8 * 8 + e], p.scale_log2, -m_use));
+        const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
+        st_shared_v4(prow + blk * 16384 + ch * 16, pack_bf16x2(pv[0], pv[1]),
+                     pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
+                     pack_bf16x2(pv[6], pv[7]));
+      }
+      if (c > 0 && __any_sync(0xffffffffu, resc)) {  // rescale O and l before PV(j) adds
+#pragma unroll
+        for (int h32 = 0; h32 < kHD / 32; ++h32) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + 256 + (i & 1) * kHD + c * 32, r);
+          tmem_ld_32x32b_x32(o_addr + h32 * 32, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            o_acc[c * 32 + e] = o_acc[c * 32 + e] * sc + __uint_as_float(r[e]);
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st_32x32b_x32(o_addr + h32 * 32, r);
         }
-        m_acc = mi;
-        tc_fence_before();
-        mbar_arrive(&o_empty[i & 1]);
+        const uint32_t lv = tmem_ld_32x32b_x1(l_addr);
+        tmem_ld_wait();
+        tmem_st_32x32b_x1(l_addr, __float_as_uint(__uint_as_float(lv) * alpha));
+        tmem_st_wait();
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
     }
-    if (ok && qi < q1) {
-      // o_acc is relative to m_acc (= last block's m_use); l_run relative to m_run
-      const float m_fin = (m_run == -INFINITY) ? 0.f : m_run;
-      const float sink = p.sinks[h] * kLog2e;
-      const float l_tot = l_run + ex2(sink - m_fin);
-      const float inv = 1.f / l_tot;
-      const float osc = ex2(m_acc - m_fin) * inv;
-      __nv_bfloat16* orow = p.out + (int64_t)qi * p.ld_out + h * kHD;
+    if (ok && c > 0) {
+      if (mbar_wait(&o_done[x], (c - 1) & 1, p.err, abort_flag)) {
+        tc_fence_after();
+        uint32_t o0[32], o1[32];
+        tmem_ld_32x32b_x32(o_addr, o0);
+        tmem_ld_32x32b_x32(o_addr + 32, o1);
+        const float l_run = __uint_as_float(tmem_ld_32x32b_x1(l_addr));
+        tmem_ld_wait();
+        if (qi < t.q1) {
+          const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+          const float l_tot = l_run + ex2(p.sinks[h] * kLog2e - m_use);
+          const float inv = 1.f / l_tot;
+          __nv_bfloat16* orow = p.out + (int64_t)qi * p.ld_out + h * kHD;
 #pragma unroll
-      for (int c8 = 0; c8 < kHD / 8; ++c8) {
-        uint4 w;
-        w.x = pack_bf16x2(o_acc[c8 * 8 + 0] * osc, o_acc[c8 * 8 + 1] * osc);
-        w.y = pack_bf16x2(o_acc[c8 * 8 + 2] * osc, o_acc[c8 * 8 + 3] * osc);
-        w.z = pack_bf16x2(o_acc[c8 * 8 + 4] * osc, o_acc[c8 * 8 + 5] * osc);
-        w.w = pack_bf16x2(o_acc[c8 * 8 + 6] * osc, o_acc[c8 * 8 + 7] * osc);
-        *reinterpret_cast<uint4*>(orow + c8 * 8) = w;
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o0[c8 * 8 + 0]) * inv, __uint_as_float(o0[c8 * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o0[c8 * 8 + 2]) * inv, __uint_as_float(o0[c8 * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o0[c8 * 8 + 4]) * inv, __uint_as_float(o0[c8 * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o0[c8 * 8 + 6]) * inv, __uint_as_float(o0[c8 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c8 * 8) = w;
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o1[c8 * 8 + 0]) * inv, __uint_as_float(o1[c8 * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o1[c8 * 8 + 2]) * inv, __uint_as_float(o1[c8 * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o1[c8 * 8 + 4]) * inv, __uint_as_float(o1[c8 * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o1[c8 * 8 + 6]) * inv, __uint_as_float(o1[c8 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + 32 + c8 * 8) = w;
+          }
+          p.lse[(int64_t)h * p.T + qi] = (m_use + __log2f(l_tot)) * kLn2;
+        }
       }
-      p.lse[(int64_t)h * p.T + qi] = (m_fin + __log2f(l_tot)) * kLn2;
     }
   }
   tc_fence_before();
@@ -355,7 +426,7 @@ void attn_fwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor tiles, torch
     attr[dev] = true;
   }
   dim3 grid((unsigned)hq, (unsigned)n_tiles);
-  attn_fwd_kernel<<<grid, kAttnThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, p);
+  attn_fwd_kernel<<<grid, kFwdThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, p);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -100,8 +100,8 @@ class ModelRunner:
                     ctx_slots.append(it.pages[p // P] * P + p % P)
                 new_in_ctx += list(range(base + it.start, base + L))
                 new_rows += list(range(*rows[i]))
-                for q0 in range(it.start, L, 128):
-                    tiles.append((base, base + q0, base + min(q0 + 128, L)))
+                for q0 in range(it.start, L, 256):   # forward kernel spans of <= 256 rows
+                    tiles.append((base, base + q0, base + min(q0 + 256, L)))
                 cu.append(base + L)
             tiles.sort(key=lambda t: -(t[2] - t[0]))
             ctx_slots_t = torch.tensor(ctx_slots, device=dev, dtype=torch.int32)

@@ -103,18 +103,21 @@ class _AttentionKernel(torch.autograd.Function):
 class AttentionPlan:
     """Host-built tile lists for one packed batch (reused by every layer of a step).
 
-    tiles: int32 [n, 3] = (seq_start, q_start, q_end) query tiles of 128 rows, heaviest first;
-    kv_tiles: int32 [m, 4] = (seq_start, seq_end, k_start, k_end) key tiles for the backward
-    pass, heaviest (most queries after them) first."""
+    tiles: int32 [n, 3] = (seq_start, q_start, q_end) query spans of up to 256 rows (the
+    forward kernel splits each into two 128-row tiles sharing the key blocks), heaviest first;
+    kv_tiles: int32 [m, 4] = (seq_start, seq_end, k_start, k_end) key tiles of 128 rows for
+    the backward pass, heaviest (most queries after them) first."""
 
     BLOCK = 128
+    SPAN = 256
 
     def __init__(self, cu_seqlens: torch.Tensor, device):
         cu = [int(x) for x in cu_seqlens.tolist()]
         tiles, kv = [], []
         for s, e in zip(cu[:-1], cu[1:]):
+            for q0 in range(s, e, self.SPAN):
+                tiles.append((s, q0, min(q0 + self.SPAN, e)))
             for q0 in range(s, e, self.BLOCK):
-                tiles.append((s, q0, min(q0 + self.BLOCK, e)))
                 kv.append((s, e, q0, min(q0 + self.BLOCK, e)))
         order = sorted(tiles, key=lambda t: -(t[2] - t[0]))  # longest causal prefix first
         self.tiles = torch.tensor(order or [(0, 0, 0)], dtype=torch.int32, device=device)
