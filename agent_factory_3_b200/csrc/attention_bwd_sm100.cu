@@ -3,17 +3,22 @@
 //
 // One CTA per (128-key tile, kv head).  It keeps K and V of its key tile in shared memory and
 // loops over every q head of the kv group and every 128-query block that can see the tile:
-//   S^T  = K Q^T        (tcgen05, M=128 keys, N=128 queries, K=64)     TMEM cols   0..127
-//   dP^T = V dO^T       (same shape)                                  TMEM cols 128..255
+//   S^T  = K Q^T        (tcgen05, M=128 keys, N=64 queries per half, K=64)  TMEM cols   0..127
+//   dP^T = V dO^T       (same shape)                                        TMEM cols 128..255
 //   P^T  = 2^(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - D[q])   (softmax warps,
 //          thread = key row, written as bf16 into 128B-swizzled shared memory)
 //   dV  += P^T dO       (A = P^T K-major, B = dO as MN-major)         TMEM cols 256..319
 //   dK  += dS^T Q       (A = dS^T, B = Q as MN-major)                 TMEM cols 320..383
-//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..447
-// dQ of each block is added to an fp32 buffer with 16-byte vector atomics; dK and dV are
-// complete at the end of the CTA (all q heads of the group were visited) and are written once
-// as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the sink gradient
-// d(sink_h) = -sum_i exp(sink_h - lse_h(i)) * D_h(i); an epilogue kernel converts dQ to bf16.
+//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..511 (x2)
+// The 128 query columns of S^T / dP^T are split into two halves, each with its own softmax
+// warpgroup (warps 4-7: queries 0-63, warps 12-15: queries 64-127) and its own TMEM
+// full/empty barriers: a half's S^T / dP^T of the next block is computed as soon as that
+// warpgroup has read the current one, so the tensor core overlaps the softmax.
+// dQ of each block is added to an fp32 buffer with 16-byte vector atomics by warps 8-11; dK
+// and dV are complete at the end of the CTA (all q heads of the group were visited) and are
+// written once as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the
+// sink gradient d(sink_h) = -sum_i exp(sink_h - lse_h(i)) * D_h(i); an epilogue kernel
+// converts dQ to bf16.
 #include "common.h"
 #include "host_utils.h"
 #include "sm100.cuh"
@@ -21,7 +26,7 @@
 namespace af3 {
 namespace attnb {
 
-constexpr int kThreads = 384;  // warps 8..11 drain dQ from TMEM
+constexpr int kThreads = 512;
 constexpr int kHD = 64;
 constexpr int kB = 128;  // keys per CTA tile, queries per block
 constexpr float kLog2e = 1.4426950408889634f;
@@ -55,11 +60,50 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void store_sw128(uint8_t* base, int row, int c8, uint4 w) {
-  // element (row, 8*c8 .. 8*c8+7) of a [128 rows x 128 cols] bf16 K-major SW128 tile made of
-  // two 64-column blocks of 16 KB
+// element (row, 8*c8 .. 8*c8+7) of a [128 rows x 128 cols] bf16 K-major SW128 tile made of
+// two 64-column blocks of 16 KB (shared-window address)
+__device__ __forceinline__ void store_sw128(uint32_t base, int row, int c8, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d) {
   const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
-  *reinterpret_cast<uint4*>(base + blk * 16384 + row * 128 + ch * 16) = w;
+  st_shared_v4(base + blk * 16384 + row * 128 + ch * 16, a, b, c, d);
+}
+
+// bf16 pairs of 8 consecutive values
+__device__ __forceinline__ void pack8(const float* v, uint32_t& a, uint32_t& b, uint32_t& c,
+                                      uint32_t& d) {
+  a = pack_bf16x2(v[0], v[1]);
+  b = pack_bf16x2(v[2], v[3]);
+  c = pack_bf16x2(v[4], v[5]);
+  d = pack_bf16x2(v[6], v[7]);
+}
+
+// P^T and dS^T of one key row over 32 query columns starting at c.  lse2 (log2 domain) and D
+// of the block's queries are in shared memory at lds (lse2[128] then D[128]); every lane reads
+// the same addresses, so the 16-byte loads are broadcasts.
+template <bool MASK>
+__device__ __forceinline__ void softmax_grad_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
+                                                   const float* lds, int c, float scale_log2,
+                                                   int key, int qb, int k1, int q_end, int window,
+                                                   float (&pr)[32], float (&dsr)[32]) {
+#pragma unroll
+  for (int e4 = 0; e4 < 8; ++e4) {
+    const float4 l4 = *reinterpret_cast<const float4*>(lds + c + e4 * 4);
+    const float4 d4 = *reinterpret_cast<const float4*>(lds + kB + c + e4 * 4);
+    const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e4 * 4 + u;
+      float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[u]));
+      if (MASK) {
+        const int qi = qb + c + e;
+        const bool vis = key < k1 && key <= qi && qi < q_end && (window == 0 || qi - key < window);
+        pv = vis ? pv : 0.f;
+      }
+      pr[e] = pv;
+      dsr[e] = pv * (__uint_as_float(dv[e]) - dd[u]);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -78,14 +122,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qdo_empty = bars + 3;  // [2]
   uint64_t* ld_full = bars + 5;    // [2]
   uint64_t* ld_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_empty = bars + 10;
-  uint64_t* p_full = bars + 11;    // [2] P^T/dS^T buffer b written
-  uint64_t* mma_done = bars + 13;  // [2] P^T/dS^T buffer b consumed
-  uint64_t* dq_full = bars + 15;   // [2]
-  uint64_t* dq_empty = bars + 17;  // [2]
-  uint64_t* final_done = bars + 19;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* s_full = bars + 9;     // [2] per query half
+  uint64_t* s_empty = bars + 11;   // [2] per query half
+  uint64_t* p_full = bars + 13;    // [2] P^T/dS^T buffer b written
+  uint64_t* mma_done = bars + 15;  // [2] P^T/dS^T buffer b consumed
+  uint64_t* dq_full = bars + 17;   // [2]
+  uint64_t* dq_empty = bars + 19;  // [2]
+  uint64_t* final_done = bars + 21;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -109,15 +153,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qdo_full[s], 1);
       mbar_init(&qdo_empty[s], 1);
       mbar_init(&ld_full[s], 32);
-      mbar_init(&ld_empty[s], 128);
-    }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&p_full[b], 128);
-      mbar_init(&mma_done[b], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ld_empty[s], 256);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+      mbar_init(&p_full[s], 256);
+      mbar_init(&mma_done[s], 1);
       mbar_init(&dq_full[s], 1);
       mbar_init(&dq_empty[s], 128);
     }
@@ -170,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------- MMA issuer --------------------------------------
     if (elect_one_sync()) {
-      constexpr uint32_t id_s = make_idesc_bf16(kB, kB, false, false);      // S^T, dP^T
+      constexpr uint32_t id_s = make_idesc_bf16(kB, kB / 2, false, false);  // S^T, dP^T halves
       constexpr uint32_t id_kv = make_idesc_bf16(kB, kHD, false, true);     // dV, dK
       constexpr uint32_t id_q = make_idesc_bf16(kB, kHD, true, true);       // dQ
       const uint32_t sK = smem_u32(smem + Smem::K), sV = smem_u32(smem + Smem::V);
@@ -180,21 +220,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it < n_it) {
           const int s = it & 1;
           if (!mbar_wait(&qdo_full[s], (it >> 1) & 1, p.err, abort_flag)) break;
-          if (!mbar_wait(s_empty, (it & 1) ^ 1, p.err, abort_flag)) break;
-          tc_fence_after();
           const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
           const uint32_t sDO = sQ + kB * kHD * 2;
+          for (int hf = 0; hf < 2 && ok; ++hf) {
+            if (!mbar_wait(&s_empty[hf], (it & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            // queries hf*64 .. hf*64+63 start 64 rows (8 KB, swizzle-atom aligned) in
 #pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            umma_f16(tmem + 0, make_smem_desc(sK + kk * 32, 16, 1024, kLayoutSW128),
-                     make_smem_desc(sQ + kk * 32, 16, 1024, kLayoutSW128), id_s, kk > 0);
-          }
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              umma_f16(tmem + hf * 64, make_smem_desc(sK + kk * 32, 16, 1024, kLayoutSW128),
+                       make_smem_desc(sQ + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128), id_s,
+                       kk > 0);
+            }
 #pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            umma_f16(tmem + 128, make_smem_desc(sV + kk * 32, 16, 1024, kLayoutSW128),
-                     make_smem_desc(sDO + kk * 32, 16, 1024, kLayoutSW128), id_s, kk > 0);
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              umma_f16(tmem + 128 + hf * 64, make_smem_desc(sV + kk * 32, 16, 1024, kLayoutSW128),
+                       make_smem_desc(sDO + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128), id_s,
+                       kk > 0);
+            }
+            umma_commit(&s_full[hf]);
           }
-          umma_commit(s_full);
+          if (!ok) break;
         }
         if (it >= 1) {
           const int j = it - 1;
@@ -232,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok) umma_commit(final_done);
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ------------------------- dQ drain (TMEM -> fp32 atomics) ------------------------
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // query row of the block
@@ -249,130 +295,96 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&dq_empty[j & 1]);
       if (qi < q_end) {
-          float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
+        float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            atomicAdd(dst + c, make_float4(__uint_as_float(v0[4 * c]) * p.scale,
-                                           __uint_as_float(v0[4 * c + 1]) * p.scale,
-                                           __uint_as_float(v0[4 * c + 2]) * p.scale,
-                                           __uint_as_float(v0[4 * c + 3]) * p.scale));
-            atomicAdd(dst + 8 + c, make_float4(__uint_as_float(v1[4 * c]) * p.scale,
-                                               __uint_as_float(v1[4 * c + 1]) * p.scale,
-                                               __uint_as_float(v1[4 * c + 2]) * p.scale,
-                                               __uint_as_float(v1[4 * c + 3]) * p.scale));
-          }
+        for (int c = 0; c < 8; ++c) {
+          atomicAdd(dst + c, make_float4(__uint_as_float(v0[4 * c]) * p.scale,
+                                         __uint_as_float(v0[4 * c + 1]) * p.scale,
+                                         __uint_as_float(v0[4 * c + 2]) * p.scale,
+                                         __uint_as_float(v0[4 * c + 3]) * p.scale));
+          atomicAdd(dst + 8 + c, make_float4(__uint_as_float(v1[4 * c]) * p.scale,
+                                             __uint_as_float(v1[4 * c + 1]) * p.scale,
+                                             __uint_as_float(v1[4 * c + 2]) * p.scale,
+                                             __uint_as_float(v1[4 * c + 3]) * p.scale));
+        }
       }
     }
   } else if (warp >= 4) {
-    // --------------------------- softmax gradient (P^T, dS^T) ---------------------------
+    // ---------------- softmax gradient (P^T, dS^T) of one half of the queries ----------
+    const int hf = warp >= 12 ? 1 : 0;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // key row of S^T
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
     const int key = k0 + r;
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
-      {
-        // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
-        if (it >= 2 && !mbar_wait(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const int s = it & 1;
-        if (!mbar_wait(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(s_full, it & 1, p.err, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const float* lse2 = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);
-        const float* Dq = lse2 + kB;
-        const int qb = k0 + (it % nqb) * kB;
-        uint8_t* pt = smem + Smem::PT + (it & 1) * kB * kB * 2;
-        uint8_t* ds = smem + Smem::DST + (it & 1) * kB * kB * 2;
-#pragma unroll 1
-        for (int c = 0; c < kB; c += 32) {
-          uint32_t sv[32], dv[32];
-          tmem_ld_32x32b_x32(tmem + lb + c, sv);
-          tmem_ld_32x32b_x32(tmem + lb + 128 + c, dv);
-          tmem_ld_wait();
-          if (c + 32 == kB) {
-            tc_fence_before();
-            mbar_arrive(s_empty);
-          }
-          float pr[32], dsr[32];
-          // every query of this 32-column chunk visible from this key row?
-          const bool all_vis = key < k1 && key <= qb + c && qb + c + 31 < q_end &&
-                               (p.window == 0 || qb + c + 31 - key < p.window);
-          if (all_vis) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float pv = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -lse2[c + e]));
-              pr[e] = pv;
-              dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int qi = qb + c + e;
-              const bool vis = key < k1 && key <= qi && qi < q_end &&
-                               (p.window == 0 || qi - key < p.window);
-              const float pv =
-                  vis ? ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -lse2[c + e])) : 0.f;
-              pr[e] = pv;
-              dsr[e] = pv * (__uint_as_float(dv[e]) - Dq[c + e]);
-            }
-          }
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            uint4 w, z;
-            w.x = pack_bf16x2(pr[q8 * 8 + 0], pr[q8 * 8 + 1]);
-            w.y = pack_bf16x2(pr[q8 * 8 + 2], pr[q8 * 8 + 3]);
-            w.z = pack_bf16x2(pr[q8 * 8 + 4], pr[q8 * 8 + 5]);
-            w.w = pack_bf16x2(pr[q8 * 8 + 6], pr[q8 * 8 + 7]);
-            z.x = pack_bf16x2(dsr[q8 * 8 + 0], dsr[q8 * 8 + 1]);
-            z.y = pack_bf16x2(dsr[q8 * 8 + 2], dsr[q8 * 8 + 3]);
-            z.z = pack_bf16x2(dsr[q8 * 8 + 4], dsr[q8 * 8 + 5]);
-            z.w = pack_bf16x2(dsr[q8 * 8 + 6], dsr[q8 * 8 + 7]);
-            store_sw128(pt, r, c / 8 + q8, w);
-            store_sw128(ds, r, c / 8 + q8, z);
-          }
-        }
-        mbar_arrive(&ld_empty[s]);
-        fence_proxy_async_smem();
-        mbar_arrive(&p_full[it & 1]);
+      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
+      if (it >= 2 && !mbar_wait(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+        ok = false;
+        break;
       }
+      const int s = it & 1;
+      if (!mbar_wait(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const float* lds = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);  // lse2, D
+      const int qb = k0 + (it % nqb) * kB;
+      const uint32_t pt = smem_u32(smem + Smem::PT + (it & 1) * kB * kB * 2);
+      const uint32_t ds = smem_u32(smem + Smem::DST + (it & 1) * kB * kB * 2);
+#pragma unroll 1
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = hf * 64 + cc * 32;  // query column of this 32-wide chunk
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lb + c, sv);
+        tmem_ld_32x32b_x32(tmem + lb + 128 + c, dv);
+        tmem_ld_wait();
+        if (cc == 1) {
+          tc_fence_before();
+          mbar_arrive(&s_empty[hf]);
+        }
+        // every query of this chunk visible from this key row?
+        const bool all_vis = key < k1 && key <= qb + c && qb + c + 31 < q_end &&
+                             (p.window == 0 || qb + c + 31 - key < p.window);
+        float pr[32], dsr[32];
+        if (all_vis)
+          softmax_grad_chunk<false>(sv, dv, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pr, dsr);
+        else
+          softmax_grad_chunk<true>(sv, dv, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pr, dsr);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          uint32_t a, b, cw, d;
+          pack8(&pr[q8 * 8], a, b, cw, d);
+          store_sw128(pt, r, c / 8 + q8, a, b, cw, d);
+          pack8(&dsr[q8 * 8], a, b, cw, d);
+          store_sw128(ds, r, c / 8 + q8, a, b, cw, d);
+        }
+      }
+      mbar_arrive(&ld_empty[s]);
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[it & 1]);
     }
     if (ok && mbar_wait(final_done, 0, p.err, abort_flag)) {
+      // half 0 writes dV, half 1 writes dK
       tc_fence_after();
-      uint32_t a0[32], a1[32], b0[32], b1[32];
-      tmem_ld_32x32b_x32(tmem + lb + 256, a0);   // dV
-      tmem_ld_32x32b_x32(tmem + lb + 288, a1);
-      tmem_ld_32x32b_x32(tmem + lb + 320, b0);   // dK
-      tmem_ld_32x32b_x32(tmem + lb + 352, b1);
+      uint32_t a0[32], a1[32];
+      tmem_ld_32x32b_x32(tmem + lb + 256 + hf * 64, a0);
+      tmem_ld_32x32b_x32(tmem + lb + 288 + hf * 64, a1);
       tmem_ld_wait();
       if (key < k1) {
-        __nv_bfloat16* dk = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + g) * kHD;
-        __nv_bfloat16* dv = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + p.hkv + g) * kHD;
+        const float sc = hf ? p.scale : 1.f;
+        __nv_bfloat16* dst = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + (hf ? 0 : p.hkv) + g) * kHD;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
+          float t[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[e] = __uint_as_float(a0[c8 * 8 + e]) * sc;
           uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 0]) * p.scale, __uint_as_float(b0[c8 * 8 + 1]) * p.scale);
-          w.y = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 2]) * p.scale, __uint_as_float(b0[c8 * 8 + 3]) * p.scale);
-          w.z = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 4]) * p.scale, __uint_as_float(b0[c8 * 8 + 5]) * p.scale);
-          w.w = pack_bf16x2(__uint_as_float(b0[c8 * 8 + 6]) * p.scale, __uint_as_float(b0[c8 * 8 + 7]) * p.scale);
-          reinterpret_cast<uint4*>(dk)[c8] = w;
-          w.x = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 0]) * p.scale, __uint_as_float(b1[c8 * 8 + 1]) * p.scale);
-          w.y = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 2]) * p.scale, __uint_as_float(b1[c8 * 8 + 3]) * p.scale);
-          w.z = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 4]) * p.scale, __uint_as_float(b1[c8 * 8 + 5]) * p.scale);
-          w.w = pack_bf16x2(__uint_as_float(b1[c8 * 8 + 6]) * p.scale, __uint_as_float(b1[c8 * 8 + 7]) * p.scale);
-          reinterpret_cast<uint4*>(dk)[4 + c8] = w;
-          w.x = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 0]), __uint_as_float(a0[c8 * 8 + 1]));
-          w.y = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 2]), __uint_as_float(a0[c8 * 8 + 3]));
-          w.z = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 4]), __uint_as_float(a0[c8 * 8 + 5]));
-          w.w = pack_bf16x2(__uint_as_float(a0[c8 * 8 + 6]), __uint_as_float(a0[c8 * 8 + 7]));
-          reinterpret_cast<uint4*>(dv)[c8] = w;
-          w.x = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 0]), __uint_as_float(a1[c8 * 8 + 1]));
-          w.y = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 2]), __uint_as_float(a1[c8 * 8 + 3]));
-          w.z = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 4]), __uint_as_float(a1[c8 * 8 + 5]));
-          w.w = pack_bf16x2(__uint_as_float(a1[c8 * 8 + 6]), __uint_as_float(a1[c8 * 8 + 7]));
-          reinterpret_cast<uint4*>(dv)[4 + c8] = w;
+          pack8(t, w.x, w.y, w.z, w.w);
+          reinterpret_cast<uint4*>(dst)[c8] = w;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[e] = __uint_as_float(a1[c8 * 8 + e]) * sc;
+          pack8(t, w.x, w.y, w.z, w.w);
+          reinterpret_cast<uint4*>(dst)[4 + c8] = w;
         }
       }
     }
