@@ -349,9 +349,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float l_run = __uint_as_float(tmem_ld_32x32b_x1(l_addr));
         tmem_ld_wait();
         if (qi < t.q1) {
-          const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-          const float l_tot = l_run + ex2(p.sinks[h] * kLog2e - m_use);
-          const float inv = 1.f / l_tot;
+          // the sink joins the max: a row whose scores all lie far below the sink would
+          // otherwise overflow 2^(sink - m)
+          const float m_use = (m_ref == -INFINITY) ? -INFINITY : m_ref;
+          const float sk = p.sinks[h] * kLog2e;
+          const float m_fin = fmaxf(m_use, sk);
+          const float a = ex2(m_use - m_fin);  // m_use = -inf -> 0 (O and l are 0 then)
+          const float l_tot = l_run * a + ex2(sk - m_fin);
+          const float inv = a / l_tot;
           __nv_bfloat16* orow = p.out + (int64_t)qi * p.ld_out + h * kHD;
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
@@ -371,7 +376,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             w.w = pack_bf16x2(__uint_as_float(o1[c8 * 8 + 6]) * inv, __uint_as_float(o1[c8 * 8 + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + 32 + c8 * 8) = w;
           }
-          p.lse[(int64_t)h * p.T + qi] = (m_use + __log2f(l_tot)) * kLn2;
+          p.lse[(int64_t)h * p.T + qi] = (m_fin + __log2f(l_tot)) * kLn2;
         }
       }
     }

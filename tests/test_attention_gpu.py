@@ -41,6 +41,26 @@ def test_attn_fwd(dev, seqlens, window):
     torch.testing.assert_close(lse.cpu(), lse_ref, rtol=1e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("window", [0, 32])
+def test_attn_fwd_large_scores(dev, window):
+    """Scores far above and below the sinks: early rows whose visible scores all lie far below
+    the sink must stay finite (the sink joins the row max)."""
+    hq, hkv, d, L = 8, 2, 64, 300
+    qkv, sinks, cu = _inputs([L], hq, hkv, d, seed=3)
+    qkv = (qkv.float() * 8).bfloat16()
+    ref, lse_ref = A.attention_reference(qkv.float(), cu, sinks, hq, hkv, d, window, return_lse=True)
+    plan = A.AttentionPlan(cu, dev)
+    out = torch.empty(L, hq * d, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(hq, L, device=dev, dtype=torch.float32)
+    A.ext().attn_fwd(qkv.to(dev), sinks.to(dev), plan.tiles, plan.cu, out, lse, hq, hkv, d,
+                     window, 1.0 / math.sqrt(d))
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(lse).all()) and bool(torch.isfinite(out.float()).all())
+    torch.testing.assert_close(lse.cpu(), lse_ref, rtol=1e-3, atol=5e-3)
+    err = (out.cpu().float() - ref).abs().max().item()
+    assert err < 0.15, err   # |v| ~ 8: a few bf16 ulps
+
+
 @pytest.mark.parametrize("seqlens,window", CASES)
 def test_attn_fwd_bwd(dev, seqlens, window):
     hq, hkv, d = 8, 2, 64

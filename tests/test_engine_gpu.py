@@ -75,16 +75,6 @@ def test_engine_greedy_gpu(dev):
                        eos_token_id=1)
     model = GptOssForCausalLM(cfg, device=dev).init_random(0).eval()
     prompt = list(range(7, 207))
-    ids = list(prompt)
-    ref = []
-    for _ in range(8):
-        with torch.no_grad():
-            t = torch.tensor(ids, device=dev)
-            h = model.forward_hidden(t, torch.arange(len(ids), device=dev),
-                                     torch.tensor([0, len(ids)], dtype=torch.int32))
-            nxt = int(model.logits(h[-1:]).argmax(-1))
-        ids.append(nxt)
-        ref.append(nxt)
     eng = Engine(model, num_pages=128, page_size=64, max_prefill_tokens=96).start()
 
     async def run():
@@ -103,9 +93,17 @@ def test_engine_greedy_gpu(dev):
         a, b = asyncio.run(run())
     finally:
         eng.stop()
-    # bf16 GEMMs differ slightly between full recompute and paged decode: compare the prefix
-    assert len(a["output_ids"]) == 8, a
-    n_same = next((i for i, (x, y) in enumerate(zip(a["output_ids"], ref)) if x != y), 8)
-    assert n_same >= 4, (a["output_ids"], ref)
+    # Teacher-forced check against a full recompute: a random-init model has near-tied logits
+    # (top-2 gaps of a few 1e-3), so compare each greedy token with the recomputed logits at
+    # its position instead of comparing token sequences.
+    out = a["output_ids"]
+    assert len(out) == 8, a
+    ids = prompt + out[:-1]
+    with torch.no_grad():
+        h = model.forward_hidden(torch.tensor(ids, device=dev), torch.arange(len(ids), device=dev),
+                                 torch.tensor([0, len(ids)], dtype=torch.int32))
+        lg = model.logits(h[len(prompt) - 1:]).float()
+    chosen = lg[torch.arange(8, device=dev), torch.tensor(out, device=dev)]
+    assert bool((chosen >= lg.max(-1).values - 0.05).all()), (out, lg.argmax(-1).tolist())
     assert b["output_ids"] == a["output_ids"]
     assert b["meta_info"]["cached_tokens"] >= 128
