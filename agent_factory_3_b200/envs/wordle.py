@@ -36,28 +36,37 @@ def score(guess: str, answer: str) -> list[str]:
 
 
 class WordleGame:
+    """One game.  Words are compared as character sequences of the answer's length, so any
+    alphabet works (kana, zhuyin); ``normalize`` and ``display`` are the language hooks."""
+
     def __init__(self, answer: str, valid: set[str]):
-        self.answer = answer.lower()
-        self.valid = {w.lower() for w in valid} | {self.answer}
+        self.answer = self.normalize(answer)
+        self.valid = {self.normalize(w) for w in valid} | {self.answer}
         self.attempts = 0
         self.won = self.lost = False
+
+    def normalize(self, word: str) -> str:
+        return word.lower().strip()
+
+    def display(self, word: str) -> str:
+        return word
 
     def state(self, **extra) -> dict:
         out = {"attempts": self.attempts, "attempts_remaining": MAX_ATTEMPTS - self.attempts,
                "won": self.won, "lost": self.lost, "game_over": self.won or self.lost}
         out.update(extra)
         if self.won or self.lost:
-            out["answer"] = self.answer
+            out["answer"] = self.display(self.answer)
         return out
 
     def guess(self, word: str) -> dict:
         if self.won or self.lost:
             return self.state(error="Game is over.")
         self.attempts += 1
-        g = word.lower().strip()
+        g = self.normalize(word)
         err = None
-        if len(g) != WORD_LENGTH:
-            err = f"Word must be exactly {WORD_LENGTH} letters."
+        if len(g) != len(self.answer):
+            err = f"Word must be exactly {len(self.answer)} letters."
         elif g not in self.valid:
             err = f"'{word}' is not in the allowed word list."
         if err:

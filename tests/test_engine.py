@@ -22,17 +22,17 @@ def tiny_model(dev="cpu", lora=None, dtype=torch.float32):
     return m
 
 
-def greedy_reference(model, prompt, n):
-    ids = list(prompt)
-    out = []
-    for _ in range(n):
-        t = torch.tensor(ids)
-        with torch.no_grad():
-            h = model.forward_hidden(t, torch.arange(len(ids)), torch.tensor([0, len(ids)], dtype=torch.int32))
-            nxt = int(model.logits(h[-1:]).argmax(-1))
-        ids.append(nxt)
-        out.append(nxt)
-    return out
+def assert_greedy(model, prompt, out, tol=1e-4):
+    """Each greedy token must be a (near-)argmax of a full recompute over prompt + out: the
+    engine thread's CPU reductions run in another order, and random-init models have
+    near-tied logits, so token sequences alone are a brittle comparison."""
+    ids = list(prompt) + list(out[:-1])
+    with torch.no_grad():
+        h = model.forward_hidden(torch.tensor(ids), torch.arange(len(ids)),
+                                 torch.tensor([0, len(ids)], dtype=torch.int32))
+        lg = model.logits(h[len(prompt) - 1:]).float()
+    chosen = lg[torch.arange(len(out)), torch.tensor(out)]
+    assert bool((chosen >= lg.max(-1).values - tol).all()), (out, lg.argmax(-1).tolist())
 
 
 def test_kv_cache_prefix_and_eviction():
@@ -81,15 +81,15 @@ def test_engine_greedy_matches_recompute_and_routing():
         r, r2, loads = asyncio.run(run())
     finally:
         eng.stop()
-    ref = greedy_reference(model, prompt, 6)
-    assert r["output_ids"] == ref
+    assert len(r["output_ids"]) == 6
+    assert_greedy(model, prompt, r["output_ids"])
     meta = r["meta_info"]
     assert meta["finish_reason"]["type"] == "length" and meta["completion_tokens"] == 6
     assert len(meta["output_token_logprobs"]) == 6 and len(meta["output_token_entropy"]) == 6
     rt = np.frombuffer(base64.b64decode(meta["routed_experts"]), dtype=np.int32)
     assert rt.size == (len(prompt) + 6 - 1) * 2 * 2
     # the second identical request hits the prefix cache and decodes the same tokens
-    assert r2["output_ids"] == ref and r2["meta_info"]["cached_tokens"] >= 32
+    assert r2["output_ids"] == r["output_ids"] and r2["meta_info"]["cached_tokens"] >= 32
     rt2 = np.frombuffer(base64.b64decode(r2["meta_info"]["routed_experts"]), dtype=np.int32)
     assert np.array_equal(rt, rt2)
     assert "num_running_reqs" in loads["loads"][0]
@@ -170,8 +170,7 @@ def test_lora_hot_swap_and_merged_reload(tmp_path):
         base, adapted, merged, bad = asyncio.run(run())
     finally:
         eng.stop()
-    ref_adapted = greedy_reference(tr.model, prompt, 5)
-    assert adapted["output_ids"] == ref_adapted
-    assert merged["output_ids"] == ref_adapted      # LoRA folded into the base weights
+    assert_greedy(tr.model, prompt, adapted["output_ids"])
+    assert_greedy(tr.model, prompt, merged["output_ids"])   # LoRA folded into the base weights
     assert merged["meta_info"]["weight_version"] == "m1"
     assert bad == 400

@@ -1,0 +1,184 @@
+"""CPU tests of the MCP environments: game rules, level generation, deadlock rules, sandbox
+isolation, and each server's tools called through the in-process MCP client."""
+import asyncio
+import json
+
+import pytest
+
+from agent_factory_3_b200.envs import minesweeper as MS
+from agent_factory_3_b200.envs import python_sandbox as PS
+from agent_factory_3_b200.envs import serper_search as SS
+from agent_factory_3_b200.envs import sokoban as SK
+from agent_factory_3_b200.envs import wordle_multilingual as WM
+from agent_factory_3_b200.rollout.mcp_client import McpClient
+
+
+def _call(server, name, args):
+    async def go():
+        async with McpClient(server) as c:
+            r = await c.call_tool(name, args)
+            return r.structuredContent if r.structuredContent is not None else json.loads(r.content[0].text)
+    return asyncio.run(go())
+
+
+# ------------------------------------------------------------------ minesweeper
+def test_minesweeper_first_click_and_no_guess():
+    for seed in range(5):
+        g = MS.MinesweeperGame(9, 9, 10, seed=seed)
+        r = g.reveal(4, 4)
+        assert r["state"] in ("playing", "won")
+        assert not any((4 + dx, 4 + dy) in g.mines for dx in (-1, 0, 1) for dy in (-1, 0, 1))
+        assert MS.solvable_without_guessing(9, 9, g.mines, (4, 4))
+
+
+def test_minesweeper_win_loss_and_text_mode():
+    g = MS.MinesweeperGame(6, 6, 5, seed=3)
+    g.reveal(0, 0)
+    safe = [(x, y) for y in range(6) for x in range(6) if (x, y) not in g.mines]
+    for c in safe:
+        if c not in g.opened:
+            r = g.reveal(*c)
+    assert r["state"] == "won" and r["early_exit"] and "*" in r["board"]
+    g2 = MS.MinesweeperGame(6, 6, 5, seed=3, text_mode=True)
+    text, meta = g2.reveal(0, 0)
+    mine = next(iter(g2.mines))
+    text, meta = g2.reveal(*mine)
+    assert meta["state"] == "lost" and meta["early_exit"] and "BOOM" in text
+    assert g2.reveal(0, 1)[1]["error"].startswith("Game is over")
+    assert MS.MinesweeperGame(3, 3, 1, seed=0).reveal(5, 5)["error"].startswith("Coordinates")
+
+
+def test_minesweeper_server_tools():
+    srv = MS.build_server(5, 5, 3, seed=1)
+    r = _call(srv, "reveal", {"x": 2, "y": 2})
+    assert r["state"] in ("playing", "won") and "board" in r
+    r = _call(srv, "reset_game", {"seed": 2})
+    assert r["message"] == "New game started." and r["mines_remaining"] == 3
+
+
+# ------------------------------------------------------------------ multilingual wordle
+def test_wordle_multilingual(tmp_path):
+    g = WM.make_game("en", target="crane")
+    r = g.guess("CRATE")
+    assert [x["status"] for x in r["results"]] == ["correct"] * 3 + ["absent", "correct"]
+    d = tmp_path / "ja"
+    d.mkdir()
+    (d / "answer_dict.json").write_text(json.dumps({"かんがえる": ["考える"], "あたらしい": ["新しい"]}))
+    (d / "valid_dict.json").write_text(json.dumps({"かんがえる": ["考える"], "あたらしい": ["新しい"],
+                                                   "たべものや": ["食べ物屋"]}))
+    g = WM.make_game("ja", data_dir=d, target="かんがえる")
+    r = g.guess("タベモノヤ")   # katakana folds to hiragana
+    assert r["guess"] == "たべものや" and "error" not in r
+    assert g.guess("あいうえおか")["error"].startswith("Word must be exactly 5")
+    r = g.guess("かんがえる")
+    assert r["won"] and r["answer"] == "かんがえる (考える)"
+    srv = WM.build_server("ja", data_dir=d, target="あたらしい")
+    assert _call(srv, "guess", {"word": "あたらしい"})["early_exit"] is True
+    with pytest.raises(ValueError):
+        WM.make_game("zh")
+
+
+# ------------------------------------------------------------------ sokoban
+def _solvable(level: SK.SokobanLevel, limit: int = 200000) -> bool:
+    """Breadth-first search over (player, boxes) states."""
+    start = (level.player, frozenset(level.boxes))
+    seen, frontier = {start}, [start]
+    while frontier and len(seen) < limit:
+        nxt = []
+        for player, boxes in frontier:
+            if boxes == level.targets:
+                return True
+            for dx, dy in SK.DIRS.values():
+                p = (player[0] + dx, player[1] + dy)
+                if p in level.walls:
+                    continue
+                b = boxes
+                if p in boxes:
+                    q = (p[0] + dx, p[1] + dy)
+                    if q in level.walls or q in boxes:
+                        continue
+                    b = (boxes - {p}) | {q}
+                s = (p, frozenset(b))
+                if s not in seen:
+                    seen.add(s)
+                    nxt.append(s)
+        frontier = nxt
+    return False
+
+
+def test_sokoban_levels_solvable_and_not_deadlocked():
+    for seed in range(6):
+        lv = SK.generate_level(7, 7, 2, seed=seed)
+        assert not lv.solved() and SK.find_deadlocks(lv) == []
+        assert _solvable(lv)
+
+
+def test_sokoban_deadlock_rules():
+    rows = ["XXXXXX",
+            "XB..TX",
+            "X....X",
+            "X.@..X",
+            "XXXXXX"]
+    walls = {(x, y) for y, r in enumerate(rows) for x, ch in enumerate(r) if ch == "X"}
+    lv = SK.SokobanLevel(walls, {(4, 1)}, {(1, 1)}, (2, 3), 6, 5)
+    reasons = SK.find_deadlocks(lv)
+    assert any("dead square" in r for r in reasons) and any("frozen" in r for r in reasons)
+    lv2 = SK.SokobanLevel(walls, {(4, 1)}, {(3, 2)}, (2, 3), 6, 5)
+    assert SK.find_deadlocks(lv2) == []
+
+
+def test_sokoban_server_moves():
+    srv = SK.build_server(7, 7, 2, seed=4)
+    st = _call(srv, "get_init_state", {})
+    assert "@" in st["text"] or "+" in st["text"]
+    r = _call(srv, "move_sequence", {"directions": ["up", "left"]})
+    assert r["step_count"] == 2 and r["move_history"] == ["up", "left"]
+    assert "error" in _call(srv, "move_sequence", {"directions": ["up"] * 6})
+
+
+# ------------------------------------------------------------------ python sandbox
+def test_python_sandbox_session():
+    s = PS.PythonSession(timeout=3, max_output_chars=50, fsize_mb=1)
+    try:
+        assert s.run("a = 2\na * 21")["result"] == "42"
+        assert s.run("a")["result"] == "2"
+        r = s.run("print('x' * 200)")
+        assert "truncated" in r["stdout"]
+        r = s.run("while True: pass")
+        assert r["restarted"] and "timed out" in r["stderr"]
+        assert not s.run("a")["ok"]           # state was lost on restart
+        # isolation checks that touch nothing outside the session's own directory
+        import os
+        r = s.run("import os\n(os.getuid(), os.getcwd())")
+        uid, cwd = eval(r["result"])
+        assert cwd == s.workdir and (uid == PS.NOBODY if os.geteuid() == 0 else uid == os.getuid())
+        r = s.run("open('big.bin', 'wb').write(b'0' * (4 << 20))")   # over the 1 MiB file limit
+        assert not r["ok"] or r["restarted"]
+    finally:
+        s.stop()
+
+
+def test_python_sandbox_server():
+    srv = PS.build_server(timeout=5, use_bwrap=False)
+    try:
+        assert _call(srv, "run_python", {"code": "import math\nmath.factorial(5)"})["result"] == "120"
+    finally:
+        srv.pool.close()
+
+
+# ------------------------------------------------------------------ serper
+def test_serper_search_with_fake_http():
+    calls = []
+
+    async def post(url, headers, payload):
+        calls.append((url, headers["X-API-KEY"], payload))
+        if url == SS.SCRAPE_URL:
+            return {"text": "y" * 100}
+        return {"organic": [{"title": "t", "link": "https://a", "snippet": "s"}]}
+
+    srv = SS.build_server(api_key="k", post=post, max_scrape_chars=10)
+    r = _call(srv, "search", {"q": "b200", "num": 500})
+    assert r["organic"][0]["link"] == "https://a" and calls[-1][2]["num"] == 100
+    r = _call(srv, "scrape_webpage", {"url": "https://a"})
+    assert r["text"] == "y" * 10 and r["truncated"]
+    assert "error" in _call(SS.build_server(api_key=""), "search", {"q": "x"})
