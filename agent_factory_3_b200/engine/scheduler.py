@@ -152,6 +152,13 @@ class Engine:
                     self._finish(r, {"type": "abort"})
                 self.running.clear()
                 self.waiting.clear()
+        elif cmd == "abort_request":       # one request (its client went away)
+            req = args[0]
+            for q in (self.running, self.waiting):
+                if req in q:
+                    q.remove(req)
+                    self._finish(req, {"type": "abort"})
+                    break
         elif cmd == "continue":
             self.paused = None
         elif cmd == "flush_cache":

@@ -66,11 +66,15 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
         req.on_output = lambda out: loop.call_soon_threadsafe(q.put_nowait, out)
         engine.submit(req)
         if not req.stream:
-            while True:
-                out = await q.get()
-                if out["finished"]:
-                    return web.json_response({"output_ids": out["output_ids"],
-                                              "meta_info": out["meta_info"]})
+            try:
+                while True:
+                    out = await q.get()
+                    if out["finished"]:
+                        return web.json_response({"output_ids": out["output_ids"],
+                                                  "meta_info": out["meta_info"]})
+            except asyncio.CancelledError:      # client went away: free the request's pages
+                engine.control("abort_request", req, wait=False)
+                raise
         resp = web.StreamResponse(headers={"Content-Type": "text/event-stream",
                                            "Cache-Control": "no-cache"})
         await resp.prepare(request)
@@ -83,7 +87,9 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
                     break
             await resp.write(b"data: [DONE]\n\n")
         except (ConnectionResetError, asyncio.CancelledError):
-            pass
+            # the client closed the stream (pause / stop / interrupt): abort the request so it
+            # stops generating and releases its pages; its prefix stays cached for a re-issue
+            engine.control("abort_request", req, wait=False)
         return resp
 
     def control(cmd, *args):
