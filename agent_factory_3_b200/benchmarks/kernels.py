@@ -5,6 +5,7 @@
     python -m agent_factory_3_b200.benchmarks.kernels --op gemm --m 16384 --n 5760 --k 2880
     python -m agent_factory_3_b200.benchmarks.kernels --op moe --tokens 32768
     python -m agent_factory_3_b200.benchmarks.kernels --op dequant --experts 128
+    python -m agent_factory_3_b200.benchmarks.kernels --op moe_decode --tokens 128 --path mxfp4
 
 Each run prints one JSON line with the time per call, the achieved TFLOP/s (or GB/s) and the
 fraction of the measured peak in MEASURED_PEAKS.json (when present).
@@ -128,9 +129,57 @@ def bench_dequant(args):
     return {"bytes": blocks.numel() + scales.numel() + out.numel() * 2, "ms": ms}
 
 
+def bench_moe_decode(args):
+    """One gpt-oss-120b MoE layer (128 experts, top-4, H = I = 2880) at decode batch sizes:
+    the MXFP4-direct path (AF3_MOE_MXFP4=1) or the dequantise + grouped GEMM path (=0).
+    Bytes = MXFP4 weights of the experts that received tokens (the roofline of decode)."""
+    from ..ops import mxfp4
+    from ..ops.moe_layer import ExpertWeights, moe_forward
+    E, K, H, I = 128, 4, 2880, 2880
+    T = args.tokens
+    g = torch.Generator(device="cuda").manual_seed(0)
+    gu_b = torch.randint(0, 256, (E, 2 * I, H // 32, 16), device="cuda", dtype=torch.uint8, generator=g)
+    gu_s = torch.randint(118, 124, (E, 2 * I, H // 32), device="cuda", dtype=torch.uint8, generator=g)
+    dn_b = torch.randint(0, 256, (E, H, I // 32, 16), device="cuda", dtype=torch.uint8, generator=g)
+    dn_s = torch.randint(118, 124, (E, H, I // 32), device="cuda", dtype=torch.uint8, generator=g)
+    ex = ExpertWeights(gu_b, gu_s, torch.zeros(E, 2 * I, device="cuda"), dn_b, dn_s,
+                       torch.zeros(E, H, device="cuda"))
+    router_w = torch.randn(E, H, device="cuda").bfloat16()
+    router_b = torch.zeros(E, device="cuda")
+    xn = torch.randn(T, H, device="cuda").bfloat16()
+    os.environ["AF3_MOE_MXFP4"] = "1" if args.path == "mxfp4" else "0"
+    with torch.no_grad():
+        logits = xn.float() @ router_w.float().t()
+        hit = torch.unique(logits.topk(K, -1).indices).numel()
+        ms = _time(lambda: moe_forward(xn, xn, router_w, router_b, ex, K), args.iters,
+                   flush_bytes=256 << 20)
+    per_expert = (2 * I * H + H * I) * 17 // 32   # e2m1 nibbles + one scale byte per 32
+    return {"bytes": hit * per_expert, "ms": ms, "experts_hit": hit}
+
+
+def bench_peer_sync(args):
+    """Fused fp32 -> bf16 cast + NVLink store of LoRA-sized tensors from GPU 0 into a staging
+    buffer on GPU 1 (the direct trainer -> engine weight sync).  Bytes = bf16 bytes stored."""
+    from ..parallel.weight_sync import PeerWriter, StagingBuffer
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("peer_sync needs two GPUs")
+    n_tensors = 64
+    per = (args.tokens * 1024) // n_tensors // 8 * 8      # --tokens = total MElements
+    shapes = {f"t{i}": (per,) for i in range(n_tensors)}
+    st = StagingBuffer.for_tensors(shapes, "cuda:1")
+    torch.cuda.set_device(0)
+    src = {k: torch.randn(*v, device="cuda:0") for k, v in shapes.items()}
+    torch.zeros(8, device="cuda:1").copy_(torch.zeros(8, device="cuda:0"))   # enable peer access
+    w = PeerWriter(st)
+    ms = _time(lambda: w.write(src, stream_sync=False), args.iters)
+    ok = bool(torch.equal(st.tensors()["t3"].cpu(), src["t3"].bfloat16().cpu()))
+    return {"bytes": per * n_tensors * 2, "ms": ms, "correct": ok}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe", "dequant"])
+    ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe", "dequant", "moe_decode",
+                                                  "peer_sync"])
     ap.add_argument("--seqlens", default="8192")
     ap.add_argument("--hq", type=int, default=64)
     ap.add_argument("--hkv", type=int, default=8)
@@ -140,6 +189,7 @@ def main():
     ap.add_argument("--k", type=int, default=2880)
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--experts", type=int, default=128)
+    ap.add_argument("--path", choices=["mxfp4", "dequant"], default="mxfp4")
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args()
     if args.op == "attn_fwd":
@@ -150,13 +200,19 @@ def main():
         r = bench_gemm(args)
     elif args.op == "dequant":
         r = bench_dequant(args)
+    elif args.op == "moe_decode":
+        r = bench_moe_decode(args)
+    elif args.op == "peer_sync":
+        r = bench_peer_sync(args)
     else:
         r = bench_moe(args)
     peak_tf, peak_bw, kind = _peaks()
     if "bytes" in r:
         gbs = r["bytes"] / (r["ms"] / 1e3) / 1e9
+        extra = {k: v for k, v in r.items() if k not in ("bytes", "ms")}
         print(json.dumps({"op": args.op, "ms": round(r["ms"], 4), "gb_per_s": round(gbs, 1),
-                          f"frac_of_{kind}_hbm": round(gbs / peak_bw, 3), "args": vars(args)}))
+                          f"frac_of_{kind}_hbm": round(gbs / peak_bw, 3), **extra,
+                          "args": vars(args)}))
         return
     tf = r["flops"] / (r["ms"] / 1e3) / 1e12
     print(json.dumps({"op": args.op, "ms": round(r["ms"], 4), "tflops": round(tf, 1),

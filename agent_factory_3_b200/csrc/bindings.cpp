@@ -16,6 +16,12 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           int64_t band, int64_t out_group_stride, int64_t max_ctas,
           c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2);
 void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
+void peer_cast_copy(torch::Tensor dst, std::vector<torch::Tensor> srcs, std::vector<int64_t> offsets);
+void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
+                    c10::optional<torch::Tensor> bias, torch::Tensor offsets, torch::Tensor counts,
+                    int64_t epi, c10::optional<torch::Tensor> row_scale, torch::Tensor out,
+                    double act_alpha, double act_limit, int64_t bn,
+                    c10::optional<torch::Tensor> lora_b, c10::optional<torch::Tensor> xa);
 void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor gates, bool replay);
 void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor offsets,
                torch::Tensor expert_counts, torch::Tensor dest, torch::Tensor row_src,
@@ -69,6 +75,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"),
         py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("K2") = 0);
   m.def("mxfp4_dequant", &af3::mxfp4_dequant);
+  m.def("peer_cast_copy", &af3::peer_cast_copy,
+        "cast fp32/bf16 tensors to bf16 and store them into a (peer) staging buffer");
+  m.def("moe_mxfp4_gemm", &af3::moe_mxfp4_gemm, "MXFP4 expert GEMM (swap-AB, few tokens/expert)",
+        py::arg("x"), py::arg("blocks"), py::arg("scales"), py::arg("bias"), py::arg("offsets"),
+        py::arg("counts"), py::arg("epi"), py::arg("row_scale"), py::arg("out"),
+        py::arg("act_alpha") = 1.702, py::arg("act_limit") = 7.0, py::arg("bn") = 32,
+        py::arg("lora_b") = py::none(), py::arg("xa") = py::none());
   m.def("moe_route", &af3::moe_route);
   m.def("moe_group", &af3::moe_group);
   m.def("gather_rows", &af3::gather_rows);

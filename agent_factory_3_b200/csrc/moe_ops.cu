@@ -11,42 +11,12 @@
 // the K selected logits, stable sort by expert id); top-k routing as in HF GptOssTopKRouter.
 #include "common.h"
 #include "host_utils.h"
+#include "mxfp4.cuh"
 #include "sm100.cuh"
 
 namespace af3 {
 
 // ------------------------------------ MXFP4 ------------------------------------------
-// e2m1 -> bf16 without a table.  For a nibble s|e1 e0|m, placing the three magnitude bits at
-// bf16 bits 8..6 (exponent bits 1..0 and the top mantissa bit) and the sign at bit 15 gives
-// the bf16 whose value is exactly e2m1(nibble) * 2^-126: e = 0 lands in the bf16 subnormal
-// range (m * 2^-127) and e > 0 in the normal range (2^(e-127) * (1 + m/2)).  Two exact
-// power-of-two multiplies (by 2^126 and by the block scale 2^(s-127)) then give the value.
-// Four packed bytes (eight values, low nibble first) -> four bf16x2 words.
-__device__ __forceinline__ uint32_t e2m1x2_to_bf16x2_unscaled(uint32_t byte) {
-  const uint32_t t = byte * 0x1001u;  // low nibble at bits 0..3, high nibble at bits 16..19
-  return ((t << 6) & 0x01C001C0u) | ((t << 12) & 0x80008000u);
-}
-
-// bf16 bits of 2^(s-127) (e8m0 scale): s = 0 is the subnormal 2^-127, s = 255 is +inf.
-__device__ __forceinline__ uint32_t e8m0_to_bf16_bits(uint32_t s) {
-  return s ? (s << 7) : 0x40u;
-}
-
-__device__ __forceinline__ uint4 e2m1x8_to_bf16x8(uint32_t w, uint32_t scale_bits) {
-  const uint32_t k2p126 = 0x7E807E80u;  // bf16x2 (2^126, 2^126)
-  const uint32_t sc2 = scale_bits | (scale_bits << 16);
-  const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&k2p126);
-  const __nv_bfloat162 sc = *reinterpret_cast<const __nv_bfloat162*>(&sc2);
-  uint32_t r[4];
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    uint32_t x = e2m1x2_to_bf16x2_unscaled((w >> (8 * b)) & 0xFFu);
-    __nv_bfloat162 v = __hmul2(__hmul2(*reinterpret_cast<__nv_bfloat162*>(&x), c), sc);
-    r[b] = *reinterpret_cast<uint32_t*>(&v);
-  }
-  return make_uint4(r[0], r[1], r[2], r[3]);
-}
-
 // One thread per 4 packed bytes (8 values, 16 output bytes): loads and stores of a warp are
 // contiguous (128 B in, 512 B out); the 4 threads of one 32-element block share its scale.
 __global__ void mxfp4_dequant_kernel(const uint32_t* __restrict__ words,

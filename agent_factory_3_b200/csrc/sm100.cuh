@@ -130,6 +130,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* desc, uint64_
       : "memory");
 }
 
+// Contiguous global -> shared bulk copy (no tensor map).  Both addresses 16-byte aligned and
+// `bytes` a multiple of 16; completion is counted on `bar` like a tiled TMA load.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Order generic-proxy shared-memory writes before async-proxy (tensor core / TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -247,6 +257,7 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 }
 
 // ------------------------------ UMMA descriptors ---------------------------------------
+// (make_idesc_f16 below: the same layout with A/B format 0 = f16)
 // Shared-memory matrix descriptor (tcgen05):
 //   [0,14)  start address >> 4      [16,30) leading byte offset >> 4
 //   [32,46) stride byte offset >> 4 [46,48) version = 1 (sm100)
@@ -288,6 +299,18 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// Instruction descriptor for kind::f16 with fp32 accumulation and f16 A/B (format code 0).
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_major,
+                                                      bool b_mn_major) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Named barrier over `count` threads (a subset of the CTA), id 1..15.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ------------------------------ small numeric helpers ----------------------------------

@@ -181,6 +181,11 @@ class Engine:
             self._load_merged(path)
             if flush:
                 self.kv.flush()
+        elif cmd == "apply_lora_params":    # staged tensors in the model's own LoRA layout
+            name, sd = args
+            self.loras[name] = ("params", sd)
+            self._apply_lora(name)
+            return True
         elif cmd == "set_lora_tensors":     # in-memory adapter (direct weight sync)
             name, sd = args
             self.loras[name] = sd
@@ -197,7 +202,14 @@ class Engine:
         return load_file(str(p / "adapter_model.safetensors"))
 
     def _apply_lora(self, name: str) -> None:
-        _load_lora_into(self.model, self.loras[name])
+        ad = self.loras[name]
+        if isinstance(ad, tuple) and ad[0] == "params":   # internal layout (GPU weight sync)
+            params = self.model.lora_param_dict()
+            with torch.no_grad():
+                for k, t in ad[1].items():
+                    params[k].copy_(t.view_as(params[k]))
+        else:
+            _load_lora_into(self.model, ad)
         self.active_lora = name
         self.runner.lora_active = True
 

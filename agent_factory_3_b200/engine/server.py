@@ -12,6 +12,8 @@ sglang_backend.py and trainer/sglang_controller.py of agent-factory-3):
   POST /update_weight_version    {"new_version"}
   POST /flush_cache
   POST /update_weights_from_disk {"model_path", "flush_cache", "weight_version"}
+  POST /lora_sync/export         CUDA IPC handle of a LoRA staging buffer (same machine)
+  POST /lora_sync/apply          {"lora_name", "weight_version", "flush_cache"}: staged -> model
   GET  /v1/loads, /health, /get_model_info, /get_server_info
 Control calls return once the engine thread has applied them, so a weight sync needs no
 fixed sleeps (the reference sleeps >= 13 s per LoRA sync waiting for sglang's asynchronous
@@ -140,6 +142,33 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
             await control("update_weight_version", body["weight_version"])
         return web.json_response({"success": True, "message": "weights updated"})
 
+    sync = {"stage": None}
+
+    async def lora_sync_export(request):
+        """CUDA IPC description of a staging buffer for the model's LoRA factors (same box)."""
+        import base64
+
+        from ..parallel.weight_sync import StagingBuffer
+        if sync["stage"] is None:
+            params = engine.model.lora_param_dict()
+            if not params:
+                return web.json_response({"success": False, "message": "model has no LoRA"}, status=400)
+            dev = next(iter(params.values())).device
+            sync["stage"] = StagingBuffer.for_tensors({k: tuple(v.shape) for k, v in params.items()}, dev)
+        return web.json_response({"success": True,
+                                  "handle": base64.b64encode(sync["stage"].export()).decode()})
+
+    async def lora_sync_apply(request):
+        body = await request.json() if request.can_read_body else {}
+        if sync["stage"] is None:
+            return web.json_response({"success": False, "message": "no staging buffer"}, status=400)
+        await control("apply_lora_params", body.get("lora_name", "policy"), sync["stage"].tensors())
+        if body.get("weight_version") is not None:
+            await control("update_weight_version", body["weight_version"])
+        if body.get("flush_cache", True):
+            await control("flush_cache")
+        return web.json_response({"success": True})
+
     async def loads(request):
         return web.json_response({"loads": [engine.loads()]})
 
@@ -157,6 +186,8 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
     app.router.add_post("/update_weight_version", weight_version)
     app.router.add_post("/flush_cache", flush)
     app.router.add_post("/update_weights_from_disk", update_weights)
+    app.router.add_post("/lora_sync/export", lora_sync_export)
+    app.router.add_post("/lora_sync/apply", lora_sync_apply)
     app.router.add_get("/v1/loads", loads)
     app.router.add_get("/health", health)
     app.router.add_get("/get_model_info", info)

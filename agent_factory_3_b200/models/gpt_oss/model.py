@@ -227,6 +227,19 @@ class GptOssForCausalLM(nn.Module):
         return self
 
     @torch.no_grad()
+    def lora_param_dict(self) -> dict:
+        """LoRA factors by internal name (``layers.{i}.self_attn.{name}`` /
+        ``layers.{i}.mlp.{name}``), in the model's own layouts -- the unit of direct GPU weight
+        sync between two copies of this model."""
+        out = {}
+        for i, layer in enumerate(self.layers):
+            for n, p in layer.self_attn.lora.items():
+                out[f"layers.{i}.self_attn.{n}"] = p
+            for n, p in layer.mlp.lora.items():
+                out[f"layers.{i}.mlp.{n}"] = p
+        return out
+
+    @torch.no_grad()
     def init_lora(self, seed: int = 0) -> "GptOssForCausalLM":
         """PEFT-style LoRA init only (A uniform(-1/sqrt(in), 1/sqrt(in)), B = 0)."""
         g = torch.Generator(device="cpu").manual_seed(seed)

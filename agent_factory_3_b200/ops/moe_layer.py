@@ -18,11 +18,14 @@ saved.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import gemm as G
 from . import moe as M
 from . import mxfp4
+from ._ext import ext, use_cuda_kernels
 
 
 class ExpertWeights:
@@ -63,6 +66,23 @@ class ExpertWeights:
     @classmethod
     def release_scratch(cls):
         cls._scratch.clear()
+
+    _f16_ok: dict = {}
+
+    def f16_exact(self) -> bool:
+        """True when every block scale s lies in [104, 140]: then each e2m1 value times
+        2^(s-127) is an exact f16 number and the MXFP4-direct kernel (which runs its tile in
+        f16) computes the same products as the bf16 dequantised weights.  Cached per tensor
+        version, so an in-place weight update is re-checked."""
+        ok = True
+        for sc in (self.gu_scales, self.dn_scales):
+            key = (sc.data_ptr(), sc._version, sc.numel())
+            v = self._f16_ok.get(key)
+            if v is None:
+                v = bool(((sc >= 104) & (sc <= 140)).all())
+                self._f16_ok[key] = v
+            ok = ok and v
+        return ok
 
 
 def _b(t):
@@ -137,10 +157,63 @@ class MoEFn(torch.autograd.Function):
                 None, None)
 
 
+def _mxfp4_direct(xn: torch.Tensor, experts: ExpertWeights, E: int, top_k: int) -> bool:
+    """Inference with few rows per expert and f16-exact scales: run the experts on the MXFP4
+    bytes directly.  AF3_MOE_MXFP4=0/1 forces the choice (the scale check still applies)."""
+    if not xn.is_cuda or not use_cuda_kernels(xn) or not experts.f16_exact():
+        return False
+    flag = os.environ.get("AF3_MOE_MXFP4")
+    if flag is not None:
+        return flag == "1"
+    if torch.is_grad_enabled():
+        return False
+    return xn.shape[0] * top_k <= 128 * E
+
+
+def _token_tile(rows: int, E: int) -> int:
+    avg = rows / max(1, E)
+    return 16 if avg <= 12 else 32 if avg <= 28 else 64 if avg <= 56 else 128
+
+
+def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, top_k: int,
+                      lora: dict | None = None, s: float = 1.0, replay_ids=None,
+                      act_alpha: float = 1.702, act_limit: float = 7.0,
+                      routing_out: list | None = None):
+    """Inference MoE that reads the MXFP4 expert weights directly (no bf16 copy): the
+    swap-AB kernel tiles 128 weight rows x the few tokens of each expert, and expert LoRA
+    (x A_e^T s) B_e^T joins the same accumulation as extra K blocks."""
+    lora = lora or {}
+    T, H = xn.shape
+    E = router_w.shape[0]
+    logits = G.matmul(xn, router_w, bias=router_b, out_dtype=torch.float32)
+    rt = M.route(logits, top_k, E, replay_ids=replay_ids)
+    if routing_out is not None:
+        routing_out.append(rt.ids)
+    x_s = M.gather_rows(xn, rt.row_src)
+    R = x_s.shape[0]
+    bn = _token_tile(T * top_k, E)
+    I2 = experts.gu_blocks.shape[1]
+    gu_A, gu_B, dn_A, dn_B = (lora.get(k) for k in ("gu_A", "gu_B", "dn_A", "dn_B"))
+    xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if gu_A is not None else None
+    h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
+    ext().moe_mxfp4_gemm(x_s, experts.gu_blocks, experts.gu_scales, experts.gu_bias, rt.offsets,
+                         rt.counts, 0, None, h, act_alpha, act_limit, bn,
+                         lora_b=_b(gu_B) if xa is not None else None, xa=xa)
+    ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if dn_A is not None else None
+    y_s = torch.empty(R, H, device=xn.device, dtype=torch.bfloat16)
+    ext().moe_mxfp4_gemm(h, experts.dn_blocks, experts.dn_scales, experts.dn_bias, rt.offsets,
+                         rt.counts, 1, rt.row_gate, y_s, act_alpha, act_limit, bn,
+                         lora_b=_b(dn_B) if ha is not None else None, xa=ha)
+    return M.combine_rows(y_s, rt.dest, top_k, residual=residual)
+
+
 def moe_forward(xn, residual, router_w, router_b, experts: ExpertWeights, top_k: int,
                 lora: dict | None = None, s: float = 1.0, replay_ids=None,
                 act_alpha: float = 1.702, act_limit: float = 7.0, routing_out: list | None = None):
     lora = lora or {}
+    if _mxfp4_direct(xn, experts, router_w.shape[0], top_k):
+        return moe_forward_mxfp4(xn, residual, router_w, router_b, experts, top_k, lora, s,
+                                 replay_ids, act_alpha, act_limit, routing_out)
     return MoEFn.apply(xn, residual, router_w, router_b, lora.get("gu_A"), lora.get("gu_B"),
                        lora.get("dn_A"), lora.get("dn_B"), experts, top_k, replay_ids, s,
                        act_alpha, act_limit, routing_out)

@@ -5,6 +5,9 @@ lora mode:   pause(abort) -> unload adapter -> load adapter -> set weight versio
              continue
 merged mode: pause(abort, or in_place without flush) -> update_weights_from_disk(version) ->
              continue
+direct mode: pause(abort) -> write the LoRA tensors straight into each engine's GPU staging
+             buffer (CUDA IPC + one NVLink kernel, no files) -> lora_sync/apply(version) ->
+             continue (engines on the trainer's machine)
 This package's engine applies each call before answering, so no waits are inserted
 (``settle_s=0``, the default).  For servers that apply commands asynchronously (sglang), pass
 ``settle_s`` to sleep between steps; the reference uses fixed sleeps of 5/3/2/1/2 s (LoRA) and
@@ -24,8 +27,9 @@ logger = logging.getLogger(__name__)
 class EngineController:
     def __init__(self, server_urls: list[str], mode: str = "lora", lora_name: str = "policy",
                  flush_cache: bool = True, settle_s: float = 0.0, timeout_s: float = 600.0):
-        if mode not in ("lora", "merged"):
-            raise ValueError("mode must be 'lora' or 'merged'")
+        if mode not in ("lora", "merged", "direct"):
+            raise ValueError("mode must be 'lora', 'merged' or 'direct'")
+        self._writers: dict = {}
         self.server_urls = list(server_urls)
         self.mode = mode
         self.lora_name = lora_name
@@ -41,6 +45,30 @@ class EngineController:
             await self._sync_lora(weight_path, weight_version)
         else:
             await self._sync_merged(weight_path, weight_version, flush)
+        self.last_sync_s = time.perf_counter() - t0
+        return self.last_sync_s
+
+    async def sync_direct(self, tensors: dict, weight_version: str) -> float:
+        """Direct GPU sync of ``tensors`` (the model's LoRA factors by internal name)."""
+        import base64
+
+        from ..parallel.weight_sync import PeerWriter
+        t0 = time.perf_counter()
+        async with aiohttp.ClientSession(timeout=self.timeout) as s:
+            for u in self.server_urls:
+                if u not in self._writers:
+                    async with s.post(f"{u}/lora_sync/export", json={}) as r:
+                        d = await r.json()
+                        if not d.get("success"):
+                            raise RuntimeError(f"lora_sync/export failed on {u}: {d}")
+                        self._writers[u] = PeerWriter(base64.b64decode(d["handle"]))
+        await self._call_all("pause_generation", {"mode": "abort"})
+        for u in self.server_urls:
+            self._writers[u].write(tensors)
+        await self._call_all("lora_sync/apply", {"lora_name": self.lora_name,
+                                                 "weight_version": weight_version,
+                                                 "flush_cache": True})
+        await self._call_all("continue_generation", {})
         self.last_sync_s = time.perf_counter() - t0
         return self.last_sync_s
 
