@@ -169,7 +169,6 @@ def bench_peer_sync(args):
     st = StagingBuffer.for_tensors(shapes, "cuda:1")
     torch.cuda.set_device(0)
     src = {k: torch.randn(*v, device="cuda:0") for k, v in shapes.items()}
-    torch.zeros(8, device="cuda:1").copy_(torch.zeros(8, device="cuda:0"))   # enable peer access
     w = PeerWriter(st)
     ms = _time(lambda: w.write(src, stream_sync=False), args.iters)
     ok = bool(torch.equal(st.tensors()["t3"].cpu(), src["t3"].bfloat16().cpu()))

@@ -1,9 +1,11 @@
-"""Rollout throughput of the built-in engine on one GPU (one-GPU slice):
-gpt-oss random-init weights with MXFP4 experts, ``--requests`` concurrent trajectories, each a
-``--prompt``-token random prompt that generates ``--gen`` tokens at temperature 1.0, paged bf16
-KV cache, continuous batching.
+"""Rollout throughput of the built-in engine: gpt-oss random-init weights with MXFP4 experts,
+``--requests`` concurrent trajectories, each a ``--prompt``-token random prompt that generates
+``--gen`` tokens at temperature 1.0, paged bf16 KV cache, continuous batching.  Under torchrun
+the engine runs tensor-parallel over the launched ranks (one GPU each; attention heads and
+experts split, partial sums reduced by the fused NVLink all-reduce + RMSNorm kernel).
 
     python -m agent_factory_3_b200.benchmarks.rollout_decode --model gpt-oss-120b --requests 128
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m agent_factory_3_b200.benchmarks.rollout_decode
 
 Prints one JSON line: wall time, generated tokens/s over the whole run, and the decode-phase
 rate (tokens/s from the moment every request has its first token until the last finishes),
@@ -13,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import threading
 import time
 
@@ -37,14 +40,38 @@ def main():
     if a.layers:
         cfg.num_hidden_layers = a.layers
         cfg.layer_types = cfg.layer_types[: a.layers]
-    dev = torch.device("cuda")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600))
+    dev = torch.device("cuda", torch.cuda.current_device())
     t0 = time.perf_counter()
     model = GptOssForCausalLM(cfg, device=dev).init_random(a.seed).eval()
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
     pages_per_req = (a.prompt + a.gen + a.page_size - 1) // a.page_size + 1
+    tp = shards = None
+    if world > 1:
+        from ..engine.tp import TPContext, broadcast_model, shard_model
+        broadcast_model(model)
+        shards = shard_model(model, rank, world, free_full=True)
+        torch.cuda.empty_cache()
+        tp = TPContext(None, cpu_group, dev, max_tokens=a.max_prefill_tokens + a.requests,
+                       hidden=cfg.hidden_size)
     eng = Engine(model, num_pages=a.requests * pages_per_req + 64, page_size=a.page_size,
-                 max_running=a.requests, max_prefill_tokens=a.max_prefill_tokens).start()
+                 max_running=a.requests, max_prefill_tokens=a.max_prefill_tokens, tp=tp,
+                 tp_shards=shards)
+    if rank != 0:
+        eng.runner.follow()
+        torch.cuda.synchronize()
+        tp.close()
+        dist.destroy_process_group()
+        return
+    eng.start()
     g = torch.Generator().manual_seed(a.seed)
     lock = threading.Lock()
     state = {"first": 0, "done": 0, "t_all_first": None, "t_end": None}
@@ -89,7 +116,13 @@ def main():
     eng.stop()
     gen = sum(len(r.output_ids) for r in reqs)
     wall = (state["t_end"] or time.perf_counter()) - t_start
-    out = {"metric": "rollout generated tokens/s (one GPU)", "model": a.model,
+    err = None
+    try:
+        from ..ops._ext import check_device_error
+        check_device_error()
+    except Exception as e:  # noqa: BLE001
+        err = str(e)[:200]
+    out = {"metric": "rollout generated tokens/s", "tp": world, "model": a.model,
            "layers": cfg.num_hidden_layers, "requests": a.requests, "prompt": a.prompt,
            "gen": a.gen, "completed": ok, "generated_tokens": gen, "wall_s": round(wall, 2),
            "gen_tok_per_s": round(gen / wall, 1), "engine_steps": steps, "init_s": round(init_s, 1)}
@@ -98,7 +131,15 @@ def main():
         out["decode_phase_s"] = round(dec, 2)
         out["decode_tok_per_s"] = round((gen - a.requests) / dec, 1) if dec > 0 else None
         out["decode_step_ms"] = round(dec / max(1, a.gen - 1) * 1000, 2)
+    if tp is not None:
+        out["fused_allreduce_calls"] = tp.fused_calls
+    if err:
+        out["device_error"] = err
     print(json.dumps(out), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        tp.close()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -16,7 +16,17 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           int64_t band, int64_t out_group_stride, int64_t max_ctas,
           c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2);
 void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
-void peer_cast_copy(torch::Tensor dst, std::vector<torch::Tensor> srcs, std::vector<int64_t> offsets);
+void peer_cast_copy(int64_t dst_ptr, int64_t dst_numel, std::vector<torch::Tensor> srcs,
+                    std::vector<int64_t> offsets);
+std::tuple<torch::Tensor, pybind11::bytes> symm_alloc(int64_t nbytes, int64_t device);
+int64_t ipc_open(pybind11::bytes handle);
+void ipc_close(int64_t ptr);
+void enable_peer_access(int64_t peer);
+void tp_allreduce_norm(std::vector<int64_t> bufs, std::vector<int64_t> flags, int64_t rank,
+                       int64_t epoch, int64_t ld_buf, c10::optional<torch::Tensor> residual,
+                       c10::optional<torch::Tensor> w, double eps, torch::Tensor out_x,
+                       c10::optional<torch::Tensor> out_n, int64_t T, int64_t H,
+                       double timeout_s);
 void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
                     c10::optional<torch::Tensor> bias, torch::Tensor offsets, torch::Tensor counts,
                     int64_t epi, c10::optional<torch::Tensor> row_scale, torch::Tensor out,
@@ -77,6 +87,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mxfp4_dequant", &af3::mxfp4_dequant);
   m.def("peer_cast_copy", &af3::peer_cast_copy,
         "cast fp32/bf16 tensors to bf16 and store them into a (peer) staging buffer");
+  m.def("symm_alloc", &af3::symm_alloc, "zeroed cudaMalloc buffer + its CUDA IPC handle");
+  m.def("ipc_open", &af3::ipc_open, "map another process's IPC buffer; returns a device pointer");
+  m.def("ipc_close", &af3::ipc_close);
+  m.def("enable_peer_access", &af3::enable_peer_access,
+        "allow kernels on the current device to access device `peer` (same process)");
+  m.def("tp_allreduce_norm", &af3::tp_allreduce_norm,
+        "one-shot NVLink all-reduce of per-rank partials + residual add + RMSNorm");
   m.def("moe_mxfp4_gemm", &af3::moe_mxfp4_gemm, "MXFP4 expert GEMM (swap-AB, few tokens/expert)",
         py::arg("x"), py::arg("blocks"), py::arg("scales"), py::arg("bias"), py::arg("offsets"),
         py::arg("counts"), py::arg("epi"), py::arg("row_scale"), py::arg("out"),

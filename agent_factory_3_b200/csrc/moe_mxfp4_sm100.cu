@@ -14,23 +14,30 @@
 // a block scale 2^(s-127) with s in [104, 140] is an exact f16 number, and bf16 activations in
 // the f16 range convert exactly -- so the products are those of the bf16 dequantised weights.
 // The host checks the scale range once per weight tensor and uses the dequantise path
-// otherwise.
+// otherwise; it also converts the token rows to f16 once (a small kernel) so that TMA can feed
+// them to the tensor core unchanged.
+//
+// The converted weight tile never touches shared memory: the tensor core reads its A operand
+// from tensor memory (tcgen05.mma with A in TMEM, two f16 per 32-bit column, row = TMEM lane),
+// and each converter thread owns one TMEM lane, so it stores its row with tcgen05.st.  Shared
+// memory carries only the packed 4-bit bytes and the token tile; a design that staged the f16
+// tile in shared memory spent 16 KB of writes and 16 KB of MMA reads per 4 KB of packed
+// weights and was bound by shared-memory bandwidth.
 //
 // Warp roles (768 threads, persistent CTAs over tiles (expert, 128-feature tile, token tile)):
-//   warp 0      TMA: packed weight rows [128 x 32 bytes] per 64-wide K block into a 16-stage
-//               ring (64 KB in flight per SM: the latency x bandwidth product of HBM)
-//   warp 3      TMA: the token tile [BN x 64] per K block into its own ring (16 stages for
-//               BN <= 32: every TMA-fed ring needs that depth to keep HBM busy).  With LoRA,
-//               ceil(r/64) more K blocks follow: the rows' x A_e^T * scale as the token tile
-//               and the expert's LoRA up-projection rows as the weight tile (loaded by the
-//               converters), so the low-rank term accumulates into the same TMEM tile
-//   warp 1      tcgen05.mma (kind::f16, M=128, N=BN, K=16 x 4 per block) into a double-
-//               buffered TMEM accumulator
-//   warps 4-19  converters: four threads per weight row expand its 64 e2m1 values (16 each) to
-//               f16 into a 4-stage ring of 128B-swizzled K-major tiles (many warps, because the
-//               e2m1 conversion has a long latency) and turn
-//               the token tile from bf16 into f16 in place; each tile's scales (one contiguous
-//               block) arrive by a bulk copy from warp 3 into a double buffer
+//   warp 0      TMA: packed weight rows [128 x 32 bytes] per 64-wide K block into a 24-stage
+//               ring (96 KB in flight per SM: the latency x bandwidth product of HBM)
+//   warp 3      TMA: the f16 token tile [BN x 64] per K block into its own ring; each tile's
+//               e8m0 scales (one contiguous block) by a bulk copy into a double buffer.  With
+//               LoRA, ceil(r/64) more K blocks follow: the rows' x A_e^T * scale as the token
+//               tile and the expert's LoRA up-projection rows as the weight tile (loaded by
+//               the converters), so the low-rank term accumulates into the same TMEM tile
+//   warp 1      tcgen05.mma (kind::f16, A from TMEM, M=128, N=BN, K=16 x 4 per block) into a
+//               double-buffered TMEM accumulator
+//   warps 4-19  converters, four groups of four warps; group g converts the K blocks
+//               it = g (mod 4), so four blocks are in flight and the conversion latency of one
+//               overlaps the others.  Thread (warp % 4, lane) owns weight row 32 (warp % 4) +
+//               lane: 32 packed bytes -> 64 f16 -> 32 TMEM columns of an 8-stage ring
 //   warps 20-23 epilogue: thread t owns feature row t; bias, then clamped SwiGLU (gate / up are
 //               interleaved rows 2i / 2i+1, partner taken with a lane shuffle) or a per-row
 //               router-gate scale; bf16 stores of Y[token, feature]
@@ -43,13 +50,16 @@ namespace af3 {
 namespace mxm {
 
 constexpr int kThreads = 768;
-constexpr int kConv = 512;  // converter threads (warps 4-19): four per weight row
+constexpr int kGroups = 4;          // converter groups of four warps (warps 4-19)
 constexpr int kMaxScaleCols = 96;   // K / 32 <= 96 (K <= 3072)
 constexpr int kBM = 128;    // weight rows per tile
-constexpr int kBK = 64;     // K per pipeline stage (one 128-byte bf16 swizzle row)
-constexpr int kAStages = 4;       // converted-weight stages (filled by the converters)
-constexpr int kPackStages = 16;   // packed-weight stages (TMA: latency x bandwidth)
+constexpr int kBK = 64;     // K per pipeline stage (one 128-byte f16 swizzle row)
+constexpr int kAStages = 8;       // converted-weight stages in TMEM (32 columns each)
+constexpr int kPackStages = 24;   // packed-weight stages (TMA: latency x bandwidth)
 constexpr int kMaxExperts = 512;
+constexpr int kTmemCols = 512;    // [0, 2 BN) accumulators, [256, 512) A stages
+constexpr int kACol = 256;
+static_assert(kPackStages % kGroups == 0 && kAStages % kGroups == 0, "ring / group mapping");
 
 enum Epi : int { kSwiglu = 0, kRowScale = 1 };
 
@@ -71,18 +81,19 @@ struct Params {
 template <int BN>
 struct Cfg {
   static constexpr int PACK = kBM * kBK / 2;        // 4 KB packed fp4
-  static constexpr int A = kBM * kBK * 2;           // 16 KB f16 (SW128)
-  static constexpr int X = BN * kBK * 2;            // token tile (SW128)
+  static constexpr int X = BN * kBK * 2;            // f16 token tile (SW128)
   static constexpr int X_STAGES = BN <= 32 ? 16 : (BN == 64 ? 8 : 4);   // TMA-filled ring
-  static constexpr int A_RING = 0;
-  static constexpr int X_RING = A_RING + kAStages * A;
+  static constexpr int X_RING = 0;
   static constexpr int PACK_RING = X_RING + X_STAGES * X;
   static constexpr int BARS = PACK_RING + kPackStages * PACK;
-  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int PREFIX = (kMaxExperts + 1) * 4;
+  // expert tile prefix, padded so the scale buffers after it stay 128-byte aligned (the bulk
+  // copy that fills them needs a 16-byte aligned destination)
+  static constexpr int PREFIX = ((kMaxExperts + 1) * 4 + 127) / 128 * 128;
   static constexpr int SCALES = kBM * kMaxScaleCols;   // one tile's e8m0 scales
   static constexpr int SMEM = 1024 + BARS + 1024 + PREFIX + 2 * SCALES;   // double-buffered
+  static_assert((BARS + 1024 + PREFIX) % 16 == 0 && SCALES % 16 == 0, "bulk copy alignment");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(2 * BN <= kACol, "accumulators overlap the A stages");
 };
 
 struct Tile {
@@ -120,8 +131,8 @@ __device__ __forceinline__ float silu_clamped(float g, float u, float alpha, flo
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_mxfp4_kernel(const __grid_constant__ CUtensorMap tma_w,   // [E][N][K/2] bytes
-                     const __grid_constant__ CUtensorMap tma_x,   // [R][K] bf16
-                     const __grid_constant__ CUtensorMap tma_x2,  // [R][r] bf16 (x A^T s)
+                     const __grid_constant__ CUtensorMap tma_x,   // [R][K] f16
+                     const __grid_constant__ CUtensorMap tma_x2,  // [R][r] f16 (x A^T s)
                      const Params p) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -153,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tma_x);
     if (p.K2 > 0) tma_prefetch_desc(&tma_x2);
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], kConv / 32);   // one elected arrive per converter warp
+      mbar_init(&a_full[s], 4);   // the four warps of the converting group
       mbar_init(&a_empty[s], 1);
     }
     for (int s = 0; s < C::X_STAGES; ++s) {
@@ -162,19 +173,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kPackStages; ++s) {
       mbar_init(&pack_full[s], 1);
-      mbar_init(&pack_empty[s], kConv / 32);
+      mbar_init(&pack_empty[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
       mbar_init(&sc_full[b], 1);
-      mbar_init(&sc_empty[b], kConv / 32);
+      mbar_init(&sc_empty[b], 4 * kGroups);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 2) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_alloc(tmem_holder, kTmemCols);
     tmem_relinquish();
   }
   if (warp == 2 && lane == 0) {
@@ -207,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 3) {
-    // ---------------------- TMA producer: token tiles (and x A^T s) -------------------
+    // ------------------- TMA producer: token tiles (and x A^T s), scales ----------------
     if (elect_one_sync()) {
       int ix = 0, tc = 0;
       bool ok = true;
@@ -245,15 +256,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem + b * BN;
         for (int kb = 0; kb < kb_n; ++kb, ++it) {
           const int sa = it % kAStages, sx = it % C::X_STAGES;
-          if (!mbar_wait(&a_full[sa], (it / kAStages) & 1, p.err, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&a_full[sa], (it / kAStages) & 1, p.err, abort_flag) ||
+              !mbar_wait(&x_full[sx], (it / C::X_STAGES) & 1, p.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + C::A_RING + sa * C::A);
+          const uint32_t a0 = tmem + kACol + sa * 32;
           const uint32_t x0 = smem_u32(smem + C::X_RING + sx * C::X);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_f16(d, make_smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
-                     make_smem_desc(x0 + kk * 32, 16, 1024, kLayoutSW128), idesc,
-                     (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_tmem_a(d, a0 + kk * 8, make_smem_desc(x0 + kk * 32, 16, 1024, kLayoutSW128),
+                            idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&a_empty[sa]);
           umma_commit(&x_empty[sx]);
@@ -263,10 +274,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4 && warp < 20) {
     // ------------------------- MXFP4 -> f16 converters --------------------------------
-    const int u = threadIdx.x - 128;           // 0..511
-    const int r = u & (kBM - 1);               // weight row of the tile
-    const int qq = u >> 7;                     // which 16-value quarter of the 64-wide block
-    const int hh = qq >> 1;                    // its 32-value scale block
+    const int g = (warp - 4) >> 2;             // group: converts the K blocks it = g (mod 4)
+    const int q = warp & 3;                    // TMEM lane quadrant this warp may access
+    const int r = q * 32 + lane;               // weight row of the tile = TMEM lane
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int kblk = p.K / 32;
     int it = 0, ip = 0, tc = 0;
     bool ok = true;
@@ -276,45 +287,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&sc_full[b], (tc >> 1) & 1, p.err, abort_flag)) break;
       const uint8_t* my_scales = tile_scales + b * C::SCALES + r * kblk;
       const int f = tl.f0 + r;
+      const bool row_ok = f < p.N;
       for (int kb = 0; kb < kb_n; ++kb, ++it) {
-        const int sa = it % kAStages, sx = it % C::X_STAGES;
-        // the A slot is free once the MMA of the block kAStages earlier has finished
+        const bool mx = kb < kb_w;
+        if ((it & (kGroups - 1)) != g) {
+          ip += mx ? 1 : 0;
+          continue;
+        }
+        const int sa = it % kAStages;
+        // the TMEM stage is free once the MMA of the block kAStages earlier has finished
         if (!mbar_wait(&a_empty[sa], ((it / kAStages) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
-        const uint32_t a0 = smem_u32(smem + C::A_RING + sa * C::A) + r * 128;
-        if (kb < kb_w) {
-          // 8 packed bytes (16 values) of row r -> two 16-byte f16 chunks
+        tc_fence_after();
+        const uint32_t ta = tmem + lane_base + kACol + sa * 32;
+        uint32_t v[16];
+        if (mx) {
+          // 32 packed bytes (64 values) of row r: two scale blocks -> 32 TMEM columns
           const int ps = ip % kPackStages;
           if (!mbar_wait(&pack_full[ps], (ip / kPackStages) & 1, p.err, abort_flag)) { ok = false; break; }
-          const uint2 w = *reinterpret_cast<const uint2*>(smem + C::PACK_RING + ps * C::PACK +
-                                                          r * 32 + qq * 8);
-          const uint32_t sc = e8m0_to_f16_bits(f < p.N ? my_scales[2 * kb + hh] : 127u);
-          const uint4 v0 = e2m1x8_to_f16x8(w.x, sc);
-          const uint4 v1 = e2m1x8_to_f16x8(w.y, sc);
+          const uint4* src = reinterpret_cast<const uint4*>(smem + C::PACK_RING + ps * C::PACK + r * 32);
+          const uint4 w0 = src[0], w1 = src[1];
           __syncwarp();                        // the warp's packed bytes are in registers
           if (lane == 0) mbar_arrive(&pack_empty[ps]);
           ++ip;
-          st_shared_v4(a0 + (((2 * qq) ^ (r & 7)) * 16), v0.x, v0.y, v0.z, v0.w);
-          st_shared_v4(a0 + (((2 * qq + 1) ^ (r & 7)) * 16), v1.x, v1.y, v1.z, v1.w);
+          const uint32_t s0 = e8m0_to_f16_bits(row_ok ? my_scales[2 * kb] : 127u);
+          const uint32_t s1 = e8m0_to_f16_bits(row_ok ? my_scales[2 * kb + 1] : 127u);
+          e2m1x32_to_f16x32(w0, s0, v);
+          tmem_st_32x32b_x16(ta, v);
+          e2m1x32_to_f16x32(w1, s1, v);
+          tmem_st_32x32b_x16(ta + 16, v);
         } else {
           // LoRA block: row f of B_e (bf16, K2 wide) -> f16; zeros past K2 and past N
-          const int k2 = (kb - kb_w) * kBK + qq * 16;
-          const __nv_bfloat16* src = p.lora_b + ((int64_t)tl.e * p.N + f) * p.K2;
+          const int k2 = (kb - kb_w) * kBK;
+          const __nv_bfloat16* src = p.lora_b + ((int64_t)tl.e * p.N + (row_ok ? f : 0)) * p.K2;
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int ch = 2 * qq + c, k = k2 + c * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (f < p.N && k < p.K2) v = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(src + k)));
-            st_shared_v4(a0 + ((ch ^ (r & 7)) * 16), v.x, v.y, v.z, v.w);
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int k = k2 + h * 32 + j * 8;
+              uint4 c = make_uint4(0, 0, 0, 0);
+              if (row_ok && k < p.K2) c = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(src + k)));
+              v[4 * j] = c.x;
+              v[4 * j + 1] = c.y;
+              v[4 * j + 2] = c.z;
+              v[4 * j + 3] = c.w;
+            }
+            tmem_st_32x32b_x16(ta + 16 * h, v);
           }
         }
-        // token tile: bf16 from TMA -> f16 in place (element positions unchanged)
-        if (!mbar_wait(&x_full[sx], (it / C::X_STAGES) & 1, p.err, abort_flag)) { ok = false; break; }
-        uint8_t* xs = smem + C::X_RING + sx * C::X;
-        for (int i = u; i < BN * 8; i += kConv) {
-          const uint4 f16 = bf16x8_to_f16x8(*reinterpret_cast<const uint4*>(xs + i * 16));
-          st_shared_v4(smem_u32(xs) + i * 16, f16.x, f16.y, f16.z, f16.w);
-        }
-        fence_proxy_async_smem();              // this thread's stores -> async proxy
+        tmem_st_wait();                        // this thread's TMEM stores have landed
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[sa]);
       }
@@ -368,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -377,6 +398,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 namespace af3 {
 namespace mxm {
+
+// Token rows bf16 -> contiguous f16 for the kernel's TMA (the tensor core reads both operands
+// of kind::f16 as f16).  Rows [R, C] with unit inner stride, C % 8 == 0.
+__global__ void rows_bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                        uint4* __restrict__ y, int64_t R, int c8) {
+  const int64_t n = R * c8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / c8, c = i - row * c8;
+    y[i] = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(x + row * ldx) + c));
+  }
+}
+
+torch::Tensor rows_to_f16(const torch::Tensor& x, cudaStream_t stream) {
+  AF3_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) % 8 == 0 && (x.stride(0) * 2) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+            "token rows must be [R, C] with C % 8 == 0 and 16-byte aligned rows");
+  auto y = torch::empty({x.size(0), x.size(1)}, x.options().dtype(torch::kHalf));
+  const int64_t n = x.size(0) * (x.size(1) / 8);
+  if (n == 0) return y;
+  const int threads = 256;
+  const int64_t grid = std::min<int64_t>((n + threads - 1) / threads, (int64_t)num_sms() * 8);
+  rows_bf16_to_f16_kernel<<<(unsigned)grid, threads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+      reinterpret_cast<uint4*>(y.data_ptr()), x.size(0), (int)(x.size(1) / 8));
+  AF3_CUDA_CHECK(cudaGetLastError());
+  return y;
+}
 
 template <int BN, int EPI>
 void launch(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tx2, const Params& p,
@@ -445,13 +494,16 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
   const uint32_t wb[3] = {kBK / 2, kBM, 1};
   const CUtensorMap tw = make_tmap(blocks.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wd, ws, wb,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const torch::Tensor x16 = rows_to_f16(x, stream);
   const uint64_t xd[2] = {(uint64_t)K, (uint64_t)x.size(0)};
-  const uint64_t xs[1] = {(uint64_t)x.stride(0) * 2};
+  const uint64_t xs[1] = {(uint64_t)K * 2};
   const uint32_t xb[2] = {kBK, (uint32_t)bn};
-  const CUtensorMap tx = make_tmap(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xd, xs, xb,
+  const CUtensorMap tx = make_tmap(x16.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xd, xs, xb,
                                    CU_TENSOR_MAP_SWIZZLE_128B);
   int64_t r = 0;
   CUtensorMap tx2 = tx;  // unused without LoRA
+  torch::Tensor xa16;     // keeps the converted xa alive until the launch is queued
   if (lora_b.has_value()) {
     AF3_CHECK(xa.has_value(), "xa is required with lora_b");
     check_cuda_bf16(*lora_b, "lora_b");
@@ -461,9 +513,10 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
                   lora_b->is_contiguous() && (r * 2) % 16 == 0, "lora_b must be [E, N, r], r % 8 == 0");
     AF3_CHECK(xa->dim() == 2 && xa->size(0) == x.size(0) && xa->size(1) == r && xa->stride(1) == 1,
               "xa must be [R, r]");
+    xa16 = rows_to_f16(*xa, stream);
     const uint64_t ad[2] = {(uint64_t)r, (uint64_t)x.size(0)};
-    const uint64_t as[1] = {(uint64_t)xa->stride(0) * 2};
-    tx2 = make_tmap(xa->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, as, xb,
+    const uint64_t as[1] = {(uint64_t)r * 2};
+    tx2 = make_tmap(xa16.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ad, as, xb,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   }
   Params p;
@@ -482,7 +535,6 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
   p.act_alpha = (float)act_alpha;
   p.act_limit = (float)act_limit;
   p.err = device_error_ptr();
-  auto stream = at::cuda::getCurrentCUDAStream();
 #define AF3_MXM(B)                                                                  \
   case B:                                                                           \
     if (epi == kSwiglu) launch<B, kSwiglu>(tw, tx, tx2, p, stream);                 \

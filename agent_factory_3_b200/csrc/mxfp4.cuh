@@ -61,6 +61,20 @@ __device__ __forceinline__ uint4 e2m1x8_to_f16x8(uint32_t w, uint32_t scale_f16_
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// 16 packed bytes (32 e2m1 values, low nibble first) times one block scale -> 16 f16x2 words
+__device__ __forceinline__ void e2m1x32_to_f16x32(uint4 w, uint32_t scale_f16_bits,
+                                                  uint32_t (&v)[16]) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 o = e2m1x8_to_f16x8(in[i], scale_f16_bits);
+    v[4 * i] = o.x;
+    v[4 * i + 1] = o.y;
+    v[4 * i + 2] = o.z;
+    v[4 * i + 3] = o.w;
+  }
+}
+
 // f16 bits of 2^(s-127): normal for s >= 113, subnormal 2^-24 * 2^(s-103) for s in [103, 112].
 __device__ __forceinline__ uint32_t e8m0_to_f16_bits(uint32_t s) {
   return s >= 113 ? ((s - 112) << 10) : (1u << (s - 103));

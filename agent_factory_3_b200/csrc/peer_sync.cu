@@ -59,15 +59,16 @@ __global__ void __launch_bounds__(256) peer_cast_copy_kernel(const Item* __restr
 
 }  // namespace psync
 
-// dst: bf16 buffer (typically a peer GPU's staging buffer mapped by CUDA IPC);
-// srcs: tensors on the current device (fp32 or bf16, contiguous, numel % 8 == 0);
-// offsets: element offset of each source in dst (multiples of 8).
-void peer_cast_copy(torch::Tensor dst, std::vector<torch::Tensor> srcs, std::vector<int64_t> offsets) {
+// dst_ptr: device address of a bf16 buffer of dst_numel elements (typically a peer GPU's staging
+// buffer opened with ipc_open on the current device); srcs: tensors on the current device (fp32
+// or bf16, contiguous, numel % 8 == 0); offsets: element offset of each source in dst
+// (multiples of 8).
+void peer_cast_copy(int64_t dst_ptr, int64_t dst_numel, std::vector<torch::Tensor> srcs,
+                    std::vector<int64_t> offsets) {
   using namespace psync;
-  AF3_CHECK(dst.scalar_type() == torch::kBFloat16 && dst.is_cuda(), "dst must be a bf16 CUDA tensor");
+  AF3_CHECK(dst_ptr != 0 && dst_ptr % 16 == 0, "dst must be a 16-byte aligned device address");
   AF3_CHECK(srcs.size() == offsets.size(), "one offset per source");
   AF3_CHECK((int64_t)srcs.size() <= kMaxItems, "too many tensors for one sync");
-  AF3_CHECK(reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0, "dst must be 16-byte aligned");
   if (srcs.empty()) return;
   const auto dev = srcs[0].device();
   const c10::cuda::CUDAGuard guard(dev);
@@ -79,7 +80,7 @@ void peer_cast_copy(torch::Tensor dst, std::vector<torch::Tensor> srcs, std::vec
     AF3_CHECK(t.scalar_type() == torch::kFloat32 || t.scalar_type() == torch::kBFloat16,
               "sources must be fp32 or bf16");
     AF3_CHECK(t.numel() % 8 == 0 && offsets[i] % 8 == 0, "sizes and offsets must be multiples of 8");
-    AF3_CHECK(offsets[i] + t.numel() <= dst.numel(), "source does not fit in dst");
+    AF3_CHECK(offsets[i] + t.numel() <= dst_numel, "source does not fit in dst");
     AF3_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "sources must be 16-byte aligned");
     items[i] = Item{t.data_ptr(), nv, offsets[i], t.scalar_type() == torch::kFloat32 ? 1 : 0};
     nv += t.numel() / 8;
@@ -94,7 +95,7 @@ void peer_cast_copy(torch::Tensor dst, std::vector<torch::Tensor> srcs, std::vec
   const int64_t grid = std::min<int64_t>((nv + threads - 1) / threads, (int64_t)num_sms() * 8);
   peer_cast_copy_kernel<<<(unsigned)grid, threads, 0, stream>>>(
       reinterpret_cast<const Item*>(d_items.data_ptr()), (int)items.size(), nv,
-      reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
+      reinterpret_cast<__nv_bfloat16*>(dst_ptr));
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -56,13 +56,12 @@ class ModelRunner:
             return None, None
         return attn._qkv_lora()
 
-    @torch.inference_mode()
-    def forward(self, items: list[StepItem]) -> StepOutput:
-        cfg = self.cfg
+    def _meta(self, items: list[StepItem]) -> "_Meta":
+        """Host-side step metadata: packed token ids / positions / KV slots, the decode rows with
+        their page tables, and the prefill contexts with their attention tiles."""
         dev = self.device
         P = self.kv.page_size
-        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        qs, kvs = cfg.q_size, cfg.kv_size
+        m = _Meta()
         ids, pos, slots, rows = [], [], [], []
         dec_idx, pre_idx = [], []
         for i, it in enumerate(items):
@@ -75,22 +74,20 @@ class ModelRunner:
                 slots.append(it.pages[p // P] * P + p % P)
             rows.append((r0, r0 + n))
             (dec_idx if (n == 1 and it.start > 0) else pre_idx).append(i)
-        N = len(ids)
-        ids_t = torch.tensor(ids, device=dev, dtype=torch.long)
-        pos_t = torch.tensor(pos, device=dev, dtype=torch.int32)
-        slots_t = torch.tensor(slots, device=dev, dtype=torch.int32)
-        # decode metadata
+        m.N, m.rows, m.dec_idx, m.pre_idx = len(ids), rows, dec_idx, pre_idx
+        m.ids_t = torch.tensor(ids, device=dev, dtype=torch.long)
+        m.pos_t = torch.tensor(pos, device=dev, dtype=torch.int32)
+        m.slots_t = torch.tensor(slots, device=dev, dtype=torch.int32)
         if dec_idx:
             maxp = max(len(items[i].pages) for i in dec_idx)
             pt = torch.zeros(len(dec_idx), maxp, dtype=torch.int32)
             for r, i in enumerate(dec_idx):
                 pt[r, :len(items[i].pages)] = torch.tensor(items[i].pages, dtype=torch.int32)
-            dec_pt = pt.to(dev)
-            dec_lens = torch.tensor([items[i].start + 1 for i in dec_idx], device=dev, dtype=torch.int32)
-            dec_rows = torch.tensor([rows[i][0] for i in dec_idx], device=dev, dtype=torch.long)
-            dec_max = int(max(items[i].start + 1 for i in dec_idx))
-        # prefill metadata: packed full contexts
-        if pre_idx:
+            m.dec_pt = pt.to(dev)
+            m.dec_lens = torch.tensor([items[i].start + 1 for i in dec_idx], device=dev, dtype=torch.int32)
+            m.dec_rows = torch.tensor([rows[i][0] for i in dec_idx], device=dev, dtype=torch.long)
+            m.dec_max = int(max(items[i].start + 1 for i in dec_idx))
+        if pre_idx:   # packed full contexts of the prefill chunks
             ctx_slots, new_in_ctx, new_rows, tiles, cu = [], [], [], [], [0]
             for i in pre_idx:
                 it = items[i]
@@ -104,62 +101,94 @@ class ModelRunner:
                     tiles.append((base, base + q0, base + min(q0 + 256, L)))
                 cu.append(base + L)
             tiles.sort(key=lambda t: -(t[2] - t[0]))
-            ctx_slots_t = torch.tensor(ctx_slots, device=dev, dtype=torch.int32)
-            new_in_ctx_t = torch.tensor(new_in_ctx, device=dev, dtype=torch.long)
-            new_rows_t = torch.tensor(new_rows, device=dev, dtype=torch.long)
-            tiles_t = torch.tensor(tiles, device=dev, dtype=torch.int32)
-            cu_t = torch.tensor(cu, device=dev, dtype=torch.int32)
-            n_ctx = cu[-1]
-        cos, sin = self.model.rope(dev)
-        x = torch.nn.functional.embedding(ids_t, self.model.embed_tokens)
-        rec: list = []
+            m.ctx_slots_t = torch.tensor(ctx_slots, device=dev, dtype=torch.int32)
+            m.new_in_ctx_t = torch.tensor(new_in_ctx, device=dev, dtype=torch.long)
+            m.new_rows_t = torch.tensor(new_rows, device=dev, dtype=torch.long)
+            m.tiles_t = torch.tensor(tiles, device=dev, dtype=torch.int32)
+            m.cu_t = torch.tensor(cu, device=dev, dtype=torch.int32)
+            m.n_ctx = cu[-1]
+        return m
+
+    def _attention(self, li: int, m: "_Meta", xn, qkv_w, qkv_b, A, B, lora_s, sinks, window,
+                   hq: int, hkv: int, pos_cos_sin) -> torch.Tensor:
+        """qkv projection, RoPE, KV store and attention of layer ``li`` for ``hq`` query and
+        ``hkv`` KV heads (all heads, or one tensor-parallel rank's slice).  Returns [N, hq*d]."""
+        d = self.cfg.head_dim
+        qs, kvs = hq * d, hkv * d
+        cos, sin = pos_cos_sin
+        dev = self.device
         scale = 1.0 / math.sqrt(d)
+        qkv = lora_linear(xn, qkv_w, qkv_b, A, B, None, lora_s)
+        apply_rope_(qkv, hq + hkv, d, m.pos_t, cos, sin)
+        kp, vp = self.kv.k[li], self.kv.v[li]
+        D.kv_store(qkv, qs, qs + kvs, m.slots_t, kp, vp)
+        o = torch.empty(m.N, qs, device=dev, dtype=qkv.dtype)
+        if m.dec_idx:
+            q = qkv.index_select(0, m.dec_rows)
+            od = D.decode_attention(q[:, :qs], kp, vp, m.dec_pt, m.dec_lens, sinks, hq, hkv,
+                                    window, scale, m.dec_max)
+            o.index_copy_(0, m.dec_rows, od)
+        if m.pre_idx:
+            ctx = torch.zeros(m.n_ctx, qkv.shape[1], device=dev, dtype=qkv.dtype)
+            D.kv_gather(ctx, qs, qs + kvs, m.ctx_slots_t, kp, vp)
+            ctx.index_copy_(0, m.new_in_ctx_t, qkv.index_select(0, m.new_rows_t))
+            if use_cuda_kernels(ctx) and d == 64:
+                oc = torch.empty(m.n_ctx, qs, device=dev, dtype=qkv.dtype)
+                lse = torch.empty(hq, m.n_ctx, device=dev, dtype=torch.float32)
+                ext().attn_fwd(ctx, sinks.float().contiguous(), m.tiles_t, m.cu_t, oc, lse, hq,
+                               hkv, d, window, scale)
+            else:
+                oc = attention_reference(ctx, m.cu_t, sinks, hq, hkv, d, window, scale)
+            o.index_copy_(0, m.new_rows_t, oc.index_select(0, m.new_in_ctx_t))
+        return o
+
+    def _finish(self, m: "_Meta", items, x, rec) -> StepOutput:
+        cfg = self.cfg
+        dev = self.device
+        routing = torch.stack(rec, dim=1).to(torch.uint8)       # [N, L, K]
+        self.kv.routing.view(-1, cfg.num_hidden_layers, cfg.num_experts_per_tok)[m.slots_t.long()] = routing
+        last = torch.tensor([r[1] - 1 for r, it in zip(m.rows, items) if it.want_logits],
+                            device=dev, dtype=torch.long)
+        if last.numel() == 0:  # only partial prefill chunks this step
+            return StepOutput(logits=torch.empty(0, cfg.vocab_size, device=dev), routing=routing,
+                              item_rows=m.rows)
+        hl = rmsnorm(x.index_select(0, last), self.model.norm, cfg.rms_norm_eps)
+        logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
+        return StepOutput(logits=logits, routing=routing, item_rows=m.rows)
+
+    @torch.inference_mode()
+    def forward(self, items: list[StepItem]) -> StepOutput:
+        cfg = self.cfg
+        m = self._meta(items)
+        rope = self.model.rope(self.device)
+        x = torch.nn.functional.embedding(m.ids_t, self.model.embed_tokens)
+        rec: list = []
         for li, layer in enumerate(self.model.layers):
-            a, m = layer.self_attn, layer.mlp
+            a, mlp = layer.self_attn, layer.mlp
             xn = rmsnorm(x, layer.input_layernorm, cfg.rms_norm_eps)
             A, B = self._qkv_lora(a)
-            qkv = lora_linear(xn, a.qkv_weight, a.qkv_bias, A, B, None, a.lora_scaling)
-            apply_rope_(qkv, hq + hkv, d, pos_t, cos, sin)
-            kp, vp = self.kv.k[li], self.kv.v[li]
-            D.kv_store(qkv, qs, qs + kvs, slots_t, kp, vp)
-            o = torch.empty(N, qs, device=dev, dtype=qkv.dtype)
-            if dec_idx:
-                q = qkv.index_select(0, dec_rows)
-                od = D.decode_attention(q[:, :qs], kp, vp, dec_pt, dec_lens, a.sinks, hq, hkv,
-                                        a.window, scale, dec_max)
-                o.index_copy_(0, dec_rows, od)
-            if pre_idx:
-                ctx = torch.zeros(n_ctx, qkv.shape[1], device=dev, dtype=qkv.dtype)
-                D.kv_gather(ctx, qs, qs + kvs, ctx_slots_t, kp, vp)
-                ctx.index_copy_(0, new_in_ctx_t, qkv.index_select(0, new_rows_t))
-                if use_cuda_kernels(ctx) and d == 64:
-                    oc = torch.empty(n_ctx, qs, device=dev, dtype=qkv.dtype)
-                    lse = torch.empty(hq, n_ctx, device=dev, dtype=torch.float32)
-                    ext().attn_fwd(ctx, a.sinks.float().contiguous(), tiles_t, cu_t, oc, lse, hq,
-                                   hkv, d, a.window, scale)
-                else:
-                    oc = attention_reference(ctx, cu_t, a.sinks, hq, hkv, d, a.window, scale)
-                o.index_copy_(0, new_rows_t, oc.index_select(0, new_in_ctx_t))
+            o = self._attention(li, m, xn, a.qkv_weight, a.qkv_bias, A, B, a.lora_scaling,
+                                a.sinks, a.window, cfg.num_attention_heads,
+                                cfg.num_key_value_heads, rope)
             oA = a.lora["o_proj_A"] if (self.lora_active and "o_proj_A" in a.lora) else None
             oB = a.lora["o_proj_B"] if (self.lora_active and "o_proj_B" in a.lora) else None
             h = lora_linear(o, a.o_weight, a.o_bias, oA, oB, x, a.lora_scaling)
             hn = rmsnorm(h, layer.post_attention_layernorm, cfg.rms_norm_eps)
             lay_rec: list = []
             if self.lora_active:
-                x = m(hn, h, None, lay_rec)
+                x = mlp(hn, h, None, lay_rec)
             else:
                 from ..ops.moe_layer import moe_forward
-                x = moe_forward(hn, h, m.router_weight, m.router_bias, m.experts(),
+                x = moe_forward(hn, h, mlp.router_weight, mlp.router_bias, mlp.experts(),
                                 cfg.num_experts_per_tok, None, 1.0, None, cfg.swiglu_alpha,
                                 cfg.swiglu_limit, lay_rec)
             rec.append(lay_rec[0])
-        routing = torch.stack(rec, dim=1).to(torch.uint8)       # [N, L, K]
-        self.kv.routing.view(-1, cfg.num_hidden_layers, cfg.num_experts_per_tok)[slots_t.long()] = routing
-        last = torch.tensor([r[1] - 1 for r, it in zip(rows, items) if it.want_logits],
-                            device=dev, dtype=torch.long)
-        if last.numel() == 0:  # only partial prefill chunks this step
-            return StepOutput(logits=torch.empty(0, cfg.vocab_size, device=dev), routing=routing,
-                              item_rows=rows)
-        hl = rmsnorm(x.index_select(0, last), self.model.norm, cfg.rms_norm_eps)
-        logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
-        return StepOutput(logits=logits, routing=routing, item_rows=rows)
+        return self._finish(m, items, x, rec)
+
+
+class _Meta:
+    """Per-step metadata shared by every layer (see ``ModelRunner._meta``)."""
+    N: int
+    rows: list
+    dec_idx: list
+    pre_idx: list

@@ -77,14 +77,23 @@ class Request:
 class Engine:
     def __init__(self, model, *, num_pages: int = 4096, page_size: int = 64,
                  max_running: int = 128, max_prefill_tokens: int = 16384,
-                 max_context_tokens: Optional[int] = None, weight_version: str = "0"):
+                 max_context_tokens: Optional[int] = None, weight_version: str = "0",
+                 tp=None, tp_shards=None):
+        """``tp``: an ``engine.tp.TPContext`` to run tensor-parallel (this process is one rank;
+        rank 0 runs the scheduler, the others call ``self.runner.follow()``)."""
         self.model = model
         cfg = model.cfg
         dev = model.embed_tokens.device
-        self.kv = PagedKVCache(cfg.num_hidden_layers, num_pages, page_size, cfg.num_key_value_heads,
-                               cfg.head_dim, cfg.num_experts_per_tok, dev,
-                               dtype=model.embed_tokens.dtype)
-        self.runner = ModelRunner(model, self.kv, lora_active=False)
+        world = tp.world if tp is not None else 1
+        self.kv = PagedKVCache(cfg.num_hidden_layers, num_pages, page_size,
+                               cfg.num_key_value_heads // world, cfg.head_dim,
+                               cfg.num_experts_per_tok, dev, dtype=model.embed_tokens.dtype)
+        if tp is not None:
+            from .tp import TPModelRunner
+            self.runner = TPModelRunner(model, self.kv, tp, tp_shards)
+        else:
+            self.runner = ModelRunner(model, self.kv, lora_active=False)
+        self.tp = tp
         self.max_running = max_running
         self.max_prefill_tokens = max_prefill_tokens
         self.max_context = max_context_tokens or cfg.max_position_embeddings
@@ -127,6 +136,8 @@ class Engine:
         self.inbox.put(("noop", None))
         if self._thread is not None:
             self._thread.join(timeout=30)
+        if self.tp is not None:
+            self.runner.stop_followers()
 
     def loads(self) -> dict:
         now = time.time()
@@ -202,6 +213,9 @@ class Engine:
         return load_file(str(p / "adapter_model.safetensors"))
 
     def _apply_lora(self, name: str) -> None:
+        if self.tp is not None and self.tp.world > 1:
+            raise NotImplementedError("LoRA adapters are not sharded for tensor parallelism; "
+                                      "serve merged weights or run the engine with TP=1")
         ad = self.loras[name]
         if isinstance(ad, tuple) and ad[0] == "params":   # internal layout (GPU weight sync)
             params = self.model.lora_param_dict()

@@ -1,0 +1,267 @@
+"""Tensor-parallel rollout engine: one process per GPU, heads and experts split over the ranks.
+
+The reference serves rollouts from sglang with ``--tp`` (examples/*/run_train.sh launch the
+server; rollout/sglang_backend.py talks to it).  Here the engine's own forward pass is split:
+
+  * attention: rank r owns query heads [r*Hq/P, (r+1)*Hq/P) and the KV heads they read
+    (GQA groups stay whole), its slice of q/k/v rows and of the o_proj input columns, and a
+    KV cache holding only its KV heads;
+  * MoE: expert parallel -- rank r owns experts [r*E/P, (r+1)*E/P); the router is replicated,
+    so every rank derives the same routing, and runs only its experts' rows;
+  * after o_proj and after the MoE combine each rank holds a partial [T, H] sum.  The GEMM /
+    combine write it straight into a buffer every rank has mapped (CUDA IPC), and one kernel
+    (``tp_allreduce_norm``) sums the partials of all ranks over NVLink, adds the residual and
+    applies the next RMSNorm -- the all-reduce is fused with the compute that follows it and
+    needs no separate copy-in;
+  * embeddings, final norm and LM head are replicated; rank 0 runs the scheduler and samples,
+    and ships each step's batch description to the other ranks (``broadcast_object_list`` on
+    a CPU group) before running its own share.
+
+On CPU (tests) or without the extension the same code runs with ``torch.distributed``
+all-reduce (gloo) in place of the fused kernel.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from ..ops import gemm as G
+from ..ops import moe as M
+from ..ops import mxfp4
+from ..ops._ext import ext, use_cuda_kernels
+from ..ops.moe_layer import ExpertWeights, _token_tile
+from ..ops.norm import rmsnorm, rmsnorm_reference
+from .model_runner import ModelRunner, StepItem, StepOutput
+
+
+@dataclass
+class LayerShard:
+    qkv_w: torch.Tensor
+    qkv_b: torch.Tensor
+    o_w: torch.Tensor
+    o_b: torch.Tensor | None       # rank 0 only: the bias is added once
+    sinks: torch.Tensor
+    window: int
+    router_w: torch.Tensor
+    router_b: torch.Tensor
+    experts: ExpertWeights         # this rank's experts
+    e0: int
+    e1: int
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+
+
+def shard_model(model, rank: int, world: int, free_full: bool = False) -> list[LayerShard]:
+    """This rank's slices of every decoder layer (copies; with ``free_full`` the full layer
+    weights are released afterwards)."""
+    cfg = model.cfg
+    hq, hkv, d, E = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, cfg.num_local_experts
+    if hq % world or hkv % world or E % world:
+        raise ValueError(f"TP={world} must divide {hq} query heads, {hkv} KV heads and {E} experts")
+    qh, kh, ne = hq // world, hkv // world, E // world
+    qs, kvs = cfg.q_size, cfg.kv_size
+    q0, q1 = rank * qh * d, (rank + 1) * qh * d
+    k0, k1 = qs + rank * kh * d, qs + (rank + 1) * kh * d
+    v0, v1 = qs + kvs + rank * kh * d, qs + kvs + (rank + 1) * kh * d
+    e0, e1 = rank * ne, (rank + 1) * ne
+    shards = []
+    with torch.no_grad():
+        for layer in model.layers:
+            a, m = layer.self_attn, layer.mlp
+            W, b = a.qkv_weight, a.qkv_bias
+            ex = ExpertWeights(m.gate_up_blocks[e0:e1].clone(), m.gate_up_scales[e0:e1].clone(),
+                               m.gate_up_bias[e0:e1].clone(), m.down_blocks[e0:e1].clone(),
+                               m.down_scales[e0:e1].clone(), m.down_bias[e0:e1].clone())
+            shards.append(LayerShard(
+                qkv_w=torch.cat([W[q0:q1], W[k0:k1], W[v0:v1]]).contiguous(),
+                qkv_b=torch.cat([b[q0:q1], b[k0:k1], b[v0:v1]]).contiguous(),
+                o_w=a.o_weight[:, q0:q1].contiguous(),
+                o_b=a.o_bias.detach().clone() if rank == 0 else None,
+                sinks=a.sinks[rank * qh:(rank + 1) * qh].detach().clone(),
+                window=a.window,
+                router_w=m.router_weight.detach(), router_b=m.router_bias.detach(),
+                experts=ex, e0=e0, e1=e1,
+                in_norm=layer.input_layernorm.detach(),
+                post_norm=layer.post_attention_layernorm.detach()))
+            if free_full:
+                for t in (a.qkv_weight, a.o_weight, m.gate_up_blocks, m.gate_up_scales,
+                          m.down_blocks, m.down_scales):
+                    t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+    return shards
+
+
+def broadcast_model(model, group=None, src: int = 0) -> None:
+    """Make every rank's weights equal to rank ``src``'s (random init or a checkpoint loaded on
+    one rank) before sharding."""
+    with torch.no_grad():
+        for t in list(model.parameters()) + list(model.buffers()):
+            dist.broadcast(t.data, group=group, group_src=src)
+
+
+class TPContext:
+    """Process-group plumbing of one tensor-parallel engine rank.
+
+    ``group``: the ranks of this engine (NCCL on GPU, gloo on CPU); ``cpu_group``: a gloo group
+    over the same ranks for the per-step batch broadcast.  With CUDA kernels available the
+    partial sums live in a ``SymmetricWorkspace`` of ``max_tokens`` x ``hidden`` bf16 rows."""
+
+    def __init__(self, group=None, cpu_group=None, device=None, max_tokens: int = 0,
+                 hidden: int = 0, timeout_s: float = 30.0):
+        self.group = group
+        self.cpu_group = cpu_group if cpu_group is not None else group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        self.timeout_s = timeout_s
+        self.symm = None
+        self.fused_calls = 0
+        if self.device.type == "cuda" and use_cuda_kernels(torch.empty(0, device=self.device)):
+            from ..parallel.symm import SymmetricWorkspace
+            self.symm = SymmetricWorkspace(max_tokens * hidden * 2, group, self.device)
+
+    # -- the partial-sum buffer the next reduction reads ----------------------------------
+    def partial_buffer(self, T: int, H: int) -> torch.Tensor:
+        if self.symm is not None:
+            return self.symm.local_set((self.symm.epoch + 1) % self.symm.sets, (T, H))
+        return torch.empty(T, H, device=self.device, dtype=torch.bfloat16)
+
+    def allreduce_norm(self, partial: torch.Tensor, residual: torch.Tensor,
+                       w: torch.Tensor | None, eps: float):
+        """x = residual + sum over ranks of ``partial`` (bf16), xn = RMSNorm(x) * w (or None)."""
+        T, H = partial.shape
+        if self.symm is not None:
+            self.symm.epoch += 1
+            s = self.symm.epoch % self.symm.sets
+            x = torch.empty(T, H, device=partial.device, dtype=torch.bfloat16)
+            xn = torch.empty_like(x) if w is not None else None
+            ext().tp_allreduce_norm(self.symm.set_ptrs(s), self.symm.flag_ptrs(), self.rank,
+                                    self.symm.epoch, H, residual.contiguous(),
+                                    None if w is None else w.float().contiguous(), eps, x, xn,
+                                    T, H, self.timeout_s)
+            self.fused_calls += 1
+            return x, xn
+        acc = partial.float()
+        dist.all_reduce(acc, group=self.group)
+        x = (residual.float() + acc).to(torch.bfloat16)
+        xn = rmsnorm_reference(x, w, eps) if w is not None else None
+        return x, xn
+
+    # -- step broadcast (rank 0 -> others) -------------------------------------------------
+    def send_items(self, items: list[StepItem] | None) -> None:
+        obj = [None if items is None else [(it.ids, it.start, it.pages, it.want_logits)
+                                           for it in items]]
+        dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
+
+    def recv_items(self) -> list[StepItem] | None:
+        obj = [None]
+        dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
+        if obj[0] is None:
+            return None
+        return [StepItem(list(i), s, list(p), w) for i, s, p, w in obj[0]]
+
+    def close(self) -> None:
+        if self.symm is not None:
+            self.symm.close()
+
+
+def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int, alpha: float,
+                   limit: float, out: torch.Tensor, routing_out: list | None = None) -> torch.Tensor:
+    """This rank's share of the MoE output: sum over the token's top-k experts that live on
+    this rank of gate * expert(x), written into ``out`` [T, H] (no residual)."""
+    T, H = xn.shape
+    logits = G.matmul(xn, sh.router_w, bias=sh.router_b, out_dtype=torch.float32)
+    rt = M.route(logits, top_k, n_experts)
+    if routing_out is not None:
+        routing_out.append(rt.ids)
+    x_s = M.gather_rows(xn, rt.row_src)
+    R = x_s.shape[0]
+    ex = sh.experts
+    y_s = torch.zeros(R, H, device=xn.device, dtype=torch.bfloat16)
+    if xn.is_cuda and use_cuda_kernels(xn) and ex.f16_exact():
+        offs = rt.offsets[sh.e0:sh.e1 + 1]
+        cnts = rt.counts[sh.e0:sh.e1]
+        I2 = ex.gu_blocks.shape[1]
+        h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
+        bn = _token_tile(T * top_k, n_experts)
+        ext().moe_mxfp4_gemm(x_s, ex.gu_blocks, ex.gu_scales, ex.gu_bias, offs, cnts, 0, None, h,
+                             alpha, limit, bn)
+        ext().moe_mxfp4_gemm(h, ex.dn_blocks, ex.dn_scales, ex.dn_bias, offs, cnts, 1,
+                             rt.row_gate, y_s, alpha, limit, bn)
+    else:
+        W_gu = mxfp4.dequantize(ex.gu_blocks, ex.gu_scales)
+        W_dn = mxfp4.dequantize(ex.dn_blocks, ex.dn_scales)
+        offs, cnts = rt.offsets.tolist(), rt.counts.tolist()
+        for e in range(sh.e0, sh.e1):
+            r0, n = offs[e], cnts[e]
+            if n == 0:
+                continue
+            j = e - sh.e0
+            gu = (x_s[r0:r0 + n].float() @ W_gu[j].float().t() + ex.gu_bias[j].float())
+            h = G.swiglu_reference(gu.to(torch.bfloat16), alpha, limit).to(torch.bfloat16)
+            y = (h.float() @ W_dn[j].float().t() + ex.dn_bias[j].float()) * rt.row_gate[r0:r0 + n, None]
+            y_s[r0:r0 + n] = y.to(torch.bfloat16)
+    return M.combine_rows(y_s, rt.dest, top_k, out=out)
+
+
+class TPModelRunner(ModelRunner):
+    """Engine forward pass over this rank's shard; see the module docstring."""
+
+    def __init__(self, model, kv, ctx: TPContext, shards: list[LayerShard] | None = None):
+        super().__init__(model, kv, lora_active=False)
+        self.ctx = ctx
+        self.shards = shards if shards is not None else shard_model(model, ctx.rank, ctx.world)
+        cfg = self.cfg
+        self.hq = cfg.num_attention_heads // ctx.world
+        self.hkv = cfg.num_key_value_heads // ctx.world
+
+    def forward(self, items: list[StepItem]) -> StepOutput:
+        if self.lora_active:
+            raise NotImplementedError("LoRA adapters are not sharded for tensor parallelism")
+        if self.ctx.rank == 0 and self.ctx.world > 1:
+            self.ctx.send_items(items)
+        return self._forward(items)
+
+    def follow(self) -> int:
+        """Non-zero ranks: run the steps rank 0 broadcasts until it sends None; returns the
+        number of steps run."""
+        n = 0
+        while True:
+            items = self.ctx.recv_items()
+            if items is None:
+                return n
+            self._forward(items)
+            n += 1
+
+    def stop_followers(self) -> None:
+        if self.ctx.rank == 0 and self.ctx.world > 1:
+            self.ctx.send_items(None)
+
+    @torch.inference_mode()
+    def _forward(self, items: list[StepItem]) -> StepOutput:
+        cfg = self.cfg
+        eps = cfg.rms_norm_eps
+        H = cfg.hidden_size
+        m = self._meta(items)
+        rope = self.model.rope(self.device)
+        x = torch.nn.functional.embedding(m.ids_t, self.model.embed_tokens)
+        xn = rmsnorm(x, self.shards[0].in_norm, eps)
+        rec: list = []
+        L = len(self.shards)
+        for li, sh in enumerate(self.shards):
+            o = self._attention(li, m, xn, sh.qkv_w, sh.qkv_b, None, None, 1.0, sh.sinks,
+                                sh.window, self.hq, self.hkv, rope)
+            part = self.ctx.partial_buffer(m.N, H)
+            G.matmul(o, sh.o_w, bias=sh.o_b, out=part)
+            h, hn = self.ctx.allreduce_norm(part, x, sh.post_norm, eps)
+            part = self.ctx.partial_buffer(m.N, H)
+            lay_rec: list = []
+            moe_ep_partial(hn, sh, cfg.num_local_experts, cfg.num_experts_per_tok,
+                           cfg.swiglu_alpha, cfg.swiglu_limit, part, lay_rec)
+            rec.append(lay_rec[0])
+            nxt = self.shards[li + 1].in_norm if li + 1 < L else None
+            x, xn = self.ctx.allreduce_norm(part, h, nxt, eps)
+        if self.ctx.rank != 0:   # only rank 0 samples
+            items = [StepItem(it.ids, it.start, it.pages, False) for it in items]
+        return self._finish(m, items, x, rec)

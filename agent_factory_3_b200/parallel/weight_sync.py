@@ -37,10 +37,16 @@ def _align8(n: int) -> int:
 
 
 class StagingBuffer:
-    """Receiver side: one flat bf16 buffer holding every synced tensor at an aligned offset."""
+    """Receiver side: one flat bf16 buffer holding every synced tensor at an aligned offset.
+    On a GPU the buffer is its own ``cudaMalloc`` so its CUDA IPC handle covers exactly it."""
 
     def __init__(self, layout: list[LayoutEntry], numel: int, device, flat: torch.Tensor | None = None):
         self.layout = layout
+        self.device = torch.device(device)
+        self._handle = None
+        if flat is None and self.device.type == "cuda" and use_cuda_kernels(torch.empty(0, device=self.device)):
+            raw, self._handle = ext().symm_alloc(numel * 2, self.device.index)
+            flat = raw.view(torch.bfloat16)
         self.flat = flat if flat is not None else torch.zeros(numel, dtype=torch.bfloat16, device=device)
         self.version = 0
 
@@ -67,23 +73,34 @@ class StagingBuffer:
     def export(self) -> bytes:
         """Picklable description (CUDA IPC handle of the buffer + layout) for another process
         on the same machine."""
-        from torch.multiprocessing.reductions import reduce_tensor
-        return pickle.dumps({"tensor": reduce_tensor(self.flat),
+        if self._handle is None:
+            raise RuntimeError("only a GPU staging buffer can be exported")
+        return pickle.dumps({"handle": bytes(self._handle),
                              "layout": [(e.name, e.offset, e.shape) for e in self.layout],
                              "numel": self.flat.numel()})
 
 
 class PeerWriter:
     """Sender side: maps a staging buffer exported by another process (or wraps a local one)
-    and writes tensors into it with the fused cast + NVLink-store kernel."""
+    and writes tensors into it with the fused cast + NVLink-store kernel.  The mapping is opened
+    on ``device`` (default: the current CUDA device), with peer access enabled for it, so the
+    writing kernel must run there."""
 
-    def __init__(self, exported: bytes | StagingBuffer):
+    def __init__(self, exported: bytes | StagingBuffer, device=None):
+        self._opened = None
         if isinstance(exported, StagingBuffer):
-            self.dst, self.layout = exported.flat, exported.layout
+            self.local = exported.flat
+            self.dst_ptr, self.dst_numel = exported.flat.data_ptr(), exported.flat.numel()
+            self.layout = exported.layout
+            self.device = exported.flat.device
         else:
             d = pickle.loads(exported)
-            fn, args = d["tensor"]
-            self.dst = fn(*args)
+            self.local = None
+            self.device = torch.device(device) if device is not None else \
+                torch.device("cuda", torch.cuda.current_device())
+            with torch.cuda.device(self.device):
+                self._opened = ext().ipc_open(d["handle"])
+            self.dst_ptr, self.dst_numel = self._opened, int(d["numel"])
             self.layout = [LayoutEntry(n, o, tuple(s)) for n, o, s in d["layout"]]
         self.offsets = {e.name: e.offset for e in self.layout}
         self.shapes = {e.name: e.shape for e in self.layout}
@@ -101,15 +118,29 @@ class PeerWriter:
             if tuple(t.shape) != self.shapes[n]:
                 raise ValueError(f"{n}: shape {tuple(t.shape)} != staged {self.shapes[n]}")
         offs = [self.offsets[n] for n in names]
-        if srcs and use_cuda_kernels(srcs[0]) and all(t.numel() % 8 == 0 for t in srcs):
+        on_gpu = bool(srcs) and srcs[0].is_cuda and use_cuda_kernels(srcs[0])
+        if on_gpu and all(t.numel() % 8 == 0 for t in srcs):
+            if self._opened is not None and srcs[0].device != self.device:
+                raise ValueError(f"sources on {srcs[0].device}, mapping opened on {self.device}")
             with torch.cuda.device(srcs[0].device):
-                ext().peer_cast_copy(self.dst, [t if t.dtype in (torch.float32, torch.bfloat16)
-                                                else t.float() for t in srcs], offs)
+                if self._opened is None and self.device != srcs[0].device:
+                    ext().enable_peer_access(self.device.index)   # same-process peer buffer
+                ext().peer_cast_copy(self.dst_ptr, self.dst_numel,
+                                     [t if t.dtype in (torch.float32, torch.bfloat16)
+                                      else t.float() for t in srcs], offs)
                 if stream_sync:
                     torch.cuda.current_stream().synchronize()
-        else:
+        elif self.local is not None:
             for t, o in zip(srcs, offs):
-                self.dst[o:o + t.numel()].copy_(t.reshape(-1).to(torch.bfloat16))
+                self.local[o:o + t.numel()].copy_(t.reshape(-1).to(torch.bfloat16))
+        else:
+            raise RuntimeError("remote staging buffers need the CUDA kernel path "
+                               "(tensor sizes must be multiples of 8)")
         n_bytes = sum(t.numel() * 2 for t in srcs)
         self.bytes_written += n_bytes
         return n_bytes
+
+    def close(self) -> None:
+        if self._opened is not None:
+            ext().ipc_close(self._opened)
+            self._opened = None

@@ -1,0 +1,149 @@
+"""Tensor-parallel pieces on two GPUs (NCCL + CUDA IPC): the fused NVLink all-reduce + residual +
+RMSNorm kernel against a PyTorch fp32 reference, repeated calls through both buffer sets, and
+the TP engine runner against the single-GPU runner on a 2-layer gpt-oss-20b."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _partial(rank, step, T, H, dev):
+    g = torch.Generator(device=dev).manual_seed(1000 * step + rank)
+    return torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+
+
+def _run_allreduce(rank, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from agent_factory_3_b200.engine.tp import TPContext
+        from agent_factory_3_b200.ops._ext import check_device_error
+        dev = torch.device("cuda", rank)
+        H = 2880
+        ctx = TPContext(None, None, dev, max_tokens=300, hidden=H, timeout_s=5.0)
+        errs = []
+        for step, T in enumerate([1, 7, 128, 300, 64]):
+            part = ctx.partial_buffer(T, H)
+            part.copy_(_partial(rank, step, T, H, dev))
+            g = torch.Generator(device=dev).manual_seed(7 + step)
+            res = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+            w = torch.rand(H, generator=g, device=dev) + 0.5
+            x, xn = ctx.allreduce_norm(part, res, w, 1e-5)
+            torch.cuda.synchronize()
+            ref = res.float() + sum(_partial(r, step, T, H, dev).float() for r in range(2))
+            xr = ref.to(torch.bfloat16)
+            xf = xr.float()
+            nr = (w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)))
+            errs.append(((x.float() - xr.float()).abs().max().item(),
+                         (xn.float() - nr).abs().max().item()))
+        check_device_error()
+        dist.barrier()
+        ctx.close()
+        q.put((rank, errs, ctx.fused_calls))
+    finally:
+        dist.destroy_process_group()
+
+
+def _two_gpus():
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_fused_allreduce_norm_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run_allreduce, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=240) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, errs, calls in outs:
+        assert calls == 5
+        for ex, en in errs:
+            assert ex <= 0.0625, errs      # one bf16 ulp at |x| ~ 8 (summation order)
+            assert en <= 0.1, errs
+
+
+def _run_engine(rank, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    cpu = dist.new_group(backend="gloo")
+    try:
+        from agent_factory_3_b200.engine.kv_cache import PagedKVCache
+        from agent_factory_3_b200.engine.model_runner import ModelRunner, StepItem
+        from agent_factory_3_b200.engine.tp import (TPContext, TPModelRunner, broadcast_model,
+                                                    shard_model)
+        from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM
+        from agent_factory_3_b200.ops._ext import check_device_error
+        dev = torch.device("cuda", rank)
+        cfg = GptOssConfig.preset("gpt-oss-20b")
+        cfg.num_hidden_layers = 2
+        cfg.layer_types = cfg.layer_types[:2]
+        model = GptOssForCausalLM(cfg, device=dev).init_random(0).eval()
+        broadcast_model(model)
+
+        def kv(world):
+            return PagedKVCache(2, 16, 64, cfg.num_key_value_heads // world, cfg.head_dim,
+                                cfg.num_experts_per_tok, dev, torch.bfloat16)
+
+        g = torch.Generator().manual_seed(3)
+        a = torch.randint(0, cfg.vocab_size, (100,), generator=g).tolist()
+        b = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()
+        steps = [[StepItem(a, 0, [0, 1]), StepItem(b, 0, [2])],
+                 [StepItem([11], 100, [0, 1]), StepItem([12], 40, [2])]]
+        ctx = TPContext(None, cpu, dev, max_tokens=256, hidden=cfg.hidden_size)
+        runner = TPModelRunner(model, kv(2), ctx, shard_model(model, rank, 2))
+        if rank == 0:
+            ref = ModelRunner(model, kv(1), lora_active=False)
+            res = []
+            for items in steps:
+                want = ref.forward(items).logits
+                got = runner.forward(items).logits
+                res.append(((got - want).abs().max().item(), want.abs().max().item(),
+                            float((got.argmax(-1) == want.argmax(-1)).float().mean())))
+            runner.stop_followers()
+        else:
+            res = runner.follow()
+        torch.cuda.synchronize()
+        check_device_error()
+        dist.barrier()
+        ctx.close()
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_tp2_runner_matches_single_gpu():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run_engine, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = dict(q.get(timeout=600) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    assert outs[1] == 2
+    for err, scale, agree in outs[0]:
+        assert err <= 0.05 * max(1.0, scale), outs[0]
