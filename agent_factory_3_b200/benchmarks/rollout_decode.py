@@ -67,8 +67,7 @@ def main():
                  tp_shards=shards)
     if rank != 0:
         eng.runner.follow()
-        torch.cuda.synchronize()
-        tp.close()
+        tp.shutdown()
         dist.destroy_process_group()
         return
     eng.start()
@@ -137,8 +136,7 @@ def main():
         out["device_error"] = err
     print(json.dumps(out), flush=True)
     if world > 1:
-        torch.cuda.synchronize()
-        tp.close()
+        tp.shutdown()
         dist.destroy_process_group()
 
 

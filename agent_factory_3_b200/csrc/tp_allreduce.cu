@@ -76,10 +76,12 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 v) {
 __global__ void __launch_bounds__(kThreads) allreduce_residual_norm_kernel(const Params p) {
   __shared__ int s_ok;
   __shared__ float s_red[kThreads / 32];
-  // 1. arrival: block 0 tells every rank (including itself) that this rank's partial is ready.
-  //    The partial was written by earlier kernels of this stream, which finished before this one
-  //    started; the system-scope fence + release store publish it to the peers.
-  if (blockIdx.x == 0 && threadIdx.x < p.world) {
+  // 1. arrival: every block tells every rank (including itself) that this rank's partial is
+  //    ready (the same epoch value, so the repeats are harmless, and no block depends on another
+  //    block of this grid being scheduled).  The partial was written by earlier kernels of this
+  //    stream, which finished before this one started; the system-scope fence + release store
+  //    publish it to the peers.
+  if (threadIdx.x < p.world) {
     __threadfence_system();
     st_release_sys(p.flags[threadIdx.x] + p.rank, p.epoch);
   }

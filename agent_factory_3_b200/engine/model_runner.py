@@ -33,13 +33,16 @@ class StepItem:
     start: int              # number of tokens already in the cache for this sequence
     pages: list[int]        # pages covering start + len(ids) tokens
     want_logits: bool = True
+    all_logits: bool = False   # logits of every new token (speculative verify), not just the last
 
 
 @dataclass
 class StepOutput:
-    logits: torch.Tensor            # [n_items, V] fp32 (last new token of each item)
+    logits: torch.Tensor            # [n_rows, V] fp32: per item with want_logits, its last new
+                                    # token, or all its new tokens when all_logits
     routing: torch.Tensor | None    # [N, L, K] uint8 of the new tokens
     item_rows: list[tuple[int, int]] = field(default_factory=list)
+    logit_offsets: list[int] = field(default_factory=list)   # first logits row of each item (-1: none)
 
 
 class ModelRunner:
@@ -147,14 +150,20 @@ class ModelRunner:
         dev = self.device
         routing = torch.stack(rec, dim=1).to(torch.uint8)       # [N, L, K]
         self.kv.routing.view(-1, cfg.num_hidden_layers, cfg.num_experts_per_tok)[m.slots_t.long()] = routing
-        last = torch.tensor([r[1] - 1 for r, it in zip(m.rows, items) if it.want_logits],
-                            device=dev, dtype=torch.long)
-        if last.numel() == 0:  # only partial prefill chunks this step
+        sel, offs = [], []
+        for (r0, r1), it in zip(m.rows, items):
+            if not it.want_logits:
+                offs.append(-1)
+                continue
+            offs.append(len(sel))
+            sel += list(range(r0, r1)) if it.all_logits else [r1 - 1]
+        if not sel:  # only partial prefill chunks this step
             return StepOutput(logits=torch.empty(0, cfg.vocab_size, device=dev), routing=routing,
-                              item_rows=m.rows)
+                              item_rows=m.rows, logit_offsets=offs)
+        last = torch.tensor(sel, device=dev, dtype=torch.long)
         hl = rmsnorm(x.index_select(0, last), self.model.norm, cfg.rms_norm_eps)
         logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
-        return StepOutput(logits=logits, routing=routing, item_rows=m.rows)
+        return StepOutput(logits=logits, routing=routing, item_rows=m.rows, logit_offsets=offs)
 
     @torch.inference_mode()
     def forward(self, items: list[StepItem]) -> StepOutput:

@@ -78,7 +78,7 @@ class Engine:
     def __init__(self, model, *, num_pages: int = 4096, page_size: int = 64,
                  max_running: int = 128, max_prefill_tokens: int = 16384,
                  max_context_tokens: Optional[int] = None, weight_version: str = "0",
-                 tp=None, tp_shards=None):
+                 tp=None, tp_shards=None, drafter=None):
         """``tp``: an ``engine.tp.TPContext`` to run tensor-parallel (this process is one rank;
         rank 0 runs the scheduler, the others call ``self.runner.follow()``)."""
         self.model = model
@@ -94,6 +94,9 @@ class Engine:
         else:
             self.runner = ModelRunner(model, self.kv, lora_active=False)
         self.tp = tp
+        self.drafter = drafter          # engine.spec drafter: speculative decoding when set
+        self.spec_verifies = 0
+        self.spec_accepted = 0
         self.max_running = max_running
         self.max_prefill_tokens = max_prefill_tokens
         self.max_context = max_context_tokens or cfg.max_position_embeddings
@@ -331,16 +334,45 @@ class Engine:
             self.kv.register(r.pages[i], h)
             r.page_hashes.append(h)
 
+    def _spec_ok(self, r: Request) -> bool:
+        return (self.drafter is not None and r.top_k <= 0 and r.top_p >= 1.0 and r.min_p <= 0)
+
+    def _append(self, r: Request, t: int, lp: float, ent: float) -> bool:
+        """Record one generated token; returns True when the request has finished."""
+        r.output_ids.append(int(t))
+        r.output_logprobs.append(float(lp))
+        r.output_entropy.append(float(ent))
+        if r.stop_token_ids and t in r.stop_token_ids:
+            r.finish_reason = {"type": "stop", "matched": int(t)}
+        elif len(r.output_ids) >= r.max_new_tokens:
+            r.finish_reason = {"type": "length"}
+        elif len(r.all_ids) >= self.max_context:
+            r.finish_reason = {"type": "length"}
+        return r.finish_reason is not None
+
     def _step(self) -> None:
         self._admit()
         if not self.running:
             return
         items, owners, budget = [], [], self.max_prefill_tokens
+        spec_reqs, spec_sizes = [], []
         for r in self.running:
             ids = r.all_ids
             pending = len(ids) - r.n_cached
             if pending <= 0:
                 continue
+            if pending == 1 and r.n_cached > 0 and self._spec_ok(r):
+                k = min(self.drafter.block, r.max_new_tokens - len(r.output_ids) - 1,
+                        self.max_context - len(ids) - 1)
+                if k > 0:
+                    try:
+                        self._ensure_page(r, r.n_cached + 1 + k)
+                    except OutOfPages:
+                        k = 0
+                if k > 0:
+                    spec_reqs.append(r)
+                    spec_sizes.append(k)
+                    continue
             n = pending if pending == 1 else min(pending, max(1, budget))
             if pending > 1:
                 if budget <= 0:
@@ -353,12 +385,20 @@ class Engine:
             items.append(StepItem(ids=ids[r.n_cached:r.n_cached + n], start=r.n_cached,
                                   pages=list(r.pages), want_logits=(r.n_cached + n == len(ids))))
             owners.append(r)
+        n_plain = len(items)
+        if spec_reqs:
+            drafts = self.drafter.propose([r.all_ids for r in spec_reqs], spec_sizes)
+            for r, d in zip(spec_reqs, drafts):
+                items.append(StepItem(ids=[r.all_ids[-1]] + list(d), start=r.n_cached,
+                                      pages=list(r.pages), want_logits=True, all_logits=True))
+                owners.append(r)
         if not items:
             return
         out = self.runner.forward(items)
         self.step_count += 1
-        sample_owners = [r for r, it in zip(owners, items) if it.want_logits]
-        for r, it in zip(owners, items):
+        plain = [i for i in range(n_plain) if items[i].want_logits]
+        sample_owners = [owners[i] for i in plain]
+        for r, it in zip(owners[:n_plain], items[:n_plain]):
             r.n_cached += len(it.ids)
         if sample_owners:
             dev = out.logits.device
@@ -367,6 +407,9 @@ class Engine:
             seeds = torch.tensor([(r.seed if r.seed is not None else r.rid) for r in sample_owners],
                                  device=dev, dtype=torch.int64)
             logits = out.logits
+            if spec_reqs:
+                logits = logits.index_select(0, torch.tensor([out.logit_offsets[i] for i in plain],
+                                                             device=dev, dtype=torch.long))
             if any(r.top_k > 0 or r.top_p < 1.0 for r in sample_owners):
                 logits = _apply_top_k_top_p(logits, sample_owners)
             steps = [len(r.output_ids) for r in sample_owners]
@@ -375,17 +418,35 @@ class Engine:
             tok, lp, ent = tok.tolist(), lp.tolist(), ent.tolist()
             self.gen_tokens_window.append((time.time(), len(tok)))
             for r, t, l, e in zip(sample_owners, tok, lp, ent):
-                r.output_ids.append(int(t))
-                r.output_logprobs.append(float(l))
-                r.output_entropy.append(float(e))
-                if r.stop_token_ids and t in r.stop_token_ids:
-                    r.finish_reason = {"type": "stop", "matched": int(t)}
-                elif len(r.output_ids) >= r.max_new_tokens:
-                    r.finish_reason = {"type": "length"}
-                elif len(r.all_ids) >= self.max_context:
-                    r.finish_reason = {"type": "length"}
+                self._append(r, t, l, e)
                 if r.stream and r.finish_reason is None:
                     self._emit(r, final=False)
+        if spec_reqs:
+            from .spec import verify_block
+            n_new = 0
+            for j, r in enumerate(spec_reqs):
+                i = n_plain + j
+                o = out.logit_offsets[i]
+                it = items[i]
+                g = None
+                if r.temperature > 0:
+                    g = torch.Generator(device=out.logits.device)
+                    g.manual_seed(((r.seed if r.seed is not None else r.rid) * 1000003
+                                   + len(r.output_ids)) % (2 ** 63))
+                a, toks, lps, ents = verify_block(out.logits[o:o + len(it.ids)], it.ids[1:],
+                                                  r.temperature, g)
+                r.n_cached += a + 1          # the last token and the accepted drafts now have KV
+                self.spec_verifies += 1
+                self.spec_accepted += a
+                for t, l, e in zip(toks, lps, ents):
+                    n_new += 1
+                    if self._append(r, t, l, e):
+                        break
+                if r.stream and r.finish_reason is None:
+                    self._emit(r, final=False)
+            self.gen_tokens_window.append((time.time(), n_new))
+            self.spec_accept_length = 1.0 + self.spec_accepted / max(1, self.spec_verifies)
+            self.spec_accept_rate = self.spec_accepted / max(1, self.spec_verifies * self.drafter.block)
         still = []
         for r in self.running:
             self._register_full_pages(r)

@@ -150,8 +150,8 @@ class TPContext:
 
     # -- step broadcast (rank 0 -> others) -------------------------------------------------
     def send_items(self, items: list[StepItem] | None) -> None:
-        obj = [None if items is None else [(it.ids, it.start, it.pages, it.want_logits)
-                                           for it in items]]
+        obj = [None if items is None else [(it.ids, it.start, it.pages, it.want_logits,
+                                            it.all_logits) for it in items]]
         dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
 
     def recv_items(self) -> list[StepItem] | None:
@@ -159,11 +159,20 @@ class TPContext:
         dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
         if obj[0] is None:
             return None
-        return [StepItem(list(i), s, list(p), w) for i, s, p, w in obj[0]]
+        return [StepItem(list(i), s, list(p), w, a) for i, s, p, w, a in obj[0]]
 
     def close(self) -> None:
         if self.symm is not None:
             self.symm.close()
+
+    def shutdown(self) -> None:
+        """Collective: wait until no rank can still be reading another rank's buffer, then
+        unmap.  Every rank must call it (a rank that exits early would free memory a peer's
+        last reduction may still be reading over NVLink)."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.cpu_group)
+        self.close()
 
 
 def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int, alpha: float,
@@ -263,5 +272,5 @@ class TPModelRunner(ModelRunner):
             nxt = self.shards[li + 1].in_norm if li + 1 < L else None
             x, xn = self.ctx.allreduce_norm(part, h, nxt, eps)
         if self.ctx.rank != 0:   # only rank 0 samples
-            items = [StepItem(it.ids, it.start, it.pages, False) for it in items]
+            items = [StepItem(it.ids, it.start, it.pages, False, False) for it in items]
         return self._finish(m, items, x, rec)

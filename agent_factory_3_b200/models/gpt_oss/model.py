@@ -187,9 +187,11 @@ class GptOssForCausalLM(nn.Module):
 
     # ------------------------------------------------------------------ init / params
     @torch.no_grad()
-    def init_random(self, seed: int = 0, std: float | None = None) -> "GptOssForCausalLM":
+    def init_random(self, seed: int = 0, std: float | None = None,
+                    keep_embeddings: bool = False) -> "GptOssForCausalLM":
         """Random-init weights (normal(0, std)), experts quantized to MXFP4; LoRA A random
-        (Kaiming-uniform like PEFT), LoRA B zero."""
+        (Kaiming-uniform like PEFT), LoRA B zero.  ``keep_embeddings`` leaves the embedding
+        and LM head untouched (a draft model sharing the target's)."""
         cfg = self.cfg
         std = cfg.initializer_range if std is None else std
         dev = self.embed_tokens.device
@@ -199,8 +201,9 @@ class GptOssForCausalLM(nn.Module):
         def randn(*shape):
             return torch.randn(*shape, generator=g, device=dev) * std
 
-        self.embed_tokens.copy_(randn(*self.embed_tokens.shape).to(dev))
-        self.lm_head.copy_(randn(*self.lm_head.shape).to(dev))
+        if not keep_embeddings:
+            self.embed_tokens.copy_(randn(*self.embed_tokens.shape).to(dev))
+            self.lm_head.copy_(randn(*self.lm_head.shape).to(dev))
         for layer in self.layers:
             a, m = layer.self_attn, layer.mlp
             a.qkv_weight.copy_(randn(*a.qkv_weight.shape).to(dev))

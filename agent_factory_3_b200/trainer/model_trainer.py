@@ -108,13 +108,32 @@ class ModelTrainer(RPCMixin):
 
     # ------------------------------------------------------------------ setup
     def _flatten_grads(self):
-        """All trainable gradients are views into one flat fp32 buffer (one collective)."""
+        """All trainable tensors and their gradients are views into one flat fp32 buffer each
+        (one collective per step).  With ``shard_optimizer_state`` and several ranks, rank r
+        owns the slice [r*S, (r+1)*S) of the flat parameters: AdamW keeps the moments of that
+        slice only, gradients are reduce-scattered into it and the updated slices all-gathered
+        back into every rank's flat parameters."""
         n = sum(p.numel() for p in self.trainable)
-        self.flat_grad = torch.zeros(n, device=self.device, dtype=torch.float32)
+        w = self.world_size if self.distributed else 1
+        self.sharded = (self.config.shard_optimizer_state and w > 1 and
+                        all(p.dtype == torch.float32 for p in self.trainable))
+        n_pad = (n + w * 8 - 1) // (w * 8) * (w * 8) if self.sharded else n
+        self.flat_grad = torch.zeros(n_pad, device=self.device, dtype=torch.float32)
+        if self.sharded:
+            self.flat_param = torch.zeros(n_pad, device=self.device, dtype=torch.float32)
         off = 0
         for p in self.trainable:
-            p.grad = self.flat_grad[off:off + p.numel()].view_as(p)
-            off += p.numel()
+            k = p.numel()
+            if self.sharded:
+                self.flat_param[off:off + k].copy_(p.detach().reshape(-1))
+                p.data = self.flat_param[off:off + k].view_as(p)
+            p.grad = self.flat_grad[off:off + k].view_as(p)
+            off += k
+        if self.sharded:
+            S = n_pad // w
+            self.shard_param = torch.nn.Parameter(self.flat_param[self.rank * S:(self.rank + 1) * S])
+            self.shard_grad = torch.zeros(S, device=self.device, dtype=torch.float32)
+            self.shard_param.grad = self.shard_grad
 
     def _create_optimizer(self):
         if self.config.optimizer_type != "AdamW":
@@ -123,7 +142,7 @@ class ModelTrainer(RPCMixin):
                   betas=(self.config.adam_beta1, self.config.adam_beta2), eps=self.config.adam_epsilon)
         if self.device.type == "cuda":
             kw["fused"] = True
-        return torch.optim.AdamW(self.trainable, **kw)
+        return torch.optim.AdamW([self.shard_param] if self.sharded else self.trainable, **kw)
 
     # ------------------------------------------------------------------ step
     def _to_device(self, batch: dict) -> dict:
@@ -173,18 +192,34 @@ class ModelTrainer(RPCMixin):
 
     def _reduce_gradients(self):
         if self.distributed and self.world_size > 1:
-            dist.all_reduce(self.flat_grad)
+            if self.sharded:
+                dist.reduce_scatter_tensor(self.shard_grad, self.flat_grad)
+            else:
+                dist.all_reduce(self.flat_grad)
 
-    def _optimizer_step(self, loss_sum: torch.Tensor, states: dict) -> dict[str, float]:
+    def _apply_gradients(self) -> torch.Tensor | None:
+        """Reduce, clip and apply this step's gradients; returns the global gradient norm
+        (device tensor) when clipping is on."""
         self._reduce_gradients()
+        g = self.shard_grad if self.sharded else self.flat_grad
         grad_norm = None
         if self.config.max_grad_norm > 0:
-            grad_norm = torch.linalg.vector_norm(self.flat_grad)
-            coef = (self.config.max_grad_norm / (grad_norm + 1e-6)).clamp(max=1.0)
-            self.flat_grad.mul_(coef)
+            if self.sharded:
+                sq = g.pow(2).sum()
+                dist.all_reduce(sq)
+                grad_norm = sq.sqrt()
+            else:
+                grad_norm = torch.linalg.vector_norm(g)
+            g.mul_((self.config.max_grad_norm / (grad_norm + 1e-6)).clamp(max=1.0))
         self.optimizer.step()
         self.lr_scheduler.step()
+        if self.sharded:
+            dist.all_gather_into_tensor(self.flat_param, self.shard_param.data)
         self.flat_grad.zero_()
+        return grad_norm
+
+    def _optimizer_step(self, loss_sum: torch.Tensor, states: dict) -> dict[str, float]:
+        grad_norm = self._apply_gradients()
         extra = torch.stack([loss_sum.detach().float(),
                              grad_norm.float() if grad_norm is not None else torch.zeros((), device=self.device)])
         red = all_reduce_metric_states(states, extra=extra)
@@ -237,13 +272,7 @@ class ModelTrainer(RPCMixin):
         batch = self._to_device(host_batch)
         loss, states = self._microbatch(batch)
         loss.backward()
-        self._reduce_gradients()
-        if self.config.max_grad_norm > 0:
-            gn = torch.linalg.vector_norm(self.flat_grad)
-            self.flat_grad.mul_((self.config.max_grad_norm / (gn + 1e-6)).clamp(max=1.0))
-        self.optimizer.step()
-        self.lr_scheduler.step()
-        self.flat_grad.zero_()
+        self._apply_gradients()
         self.step_count += 1
         return loss.detach()
 
@@ -341,16 +370,25 @@ class ModelTrainer(RPCMixin):
 
     @rpc_method(gather=False)
     def save_training_state(self, output_dir: str) -> None:
+        """Optimizer + scheduler state; a sharded optimizer writes one file per rank
+        (training_state_rank{r}.pt, each holding that rank's slice of the moments)."""
         state = {"optimizer": self.optimizer.state_dict(), "lr_scheduler": self.lr_scheduler.state_dict(),
                  "step_count": self.step_count}
-        if self.rank == 0:
-            Path(output_dir).mkdir(parents=True, exist_ok=True)
+        Path(output_dir).mkdir(parents=True, exist_ok=True)
+        if self.sharded:
+            state["world_size"] = self.world_size
+            torch.save(state, Path(output_dir) / f"training_state_rank{self.rank}.pt")
+        elif self.rank == 0:
             torch.save(state, Path(output_dir) / "training_state.pt")
 
     @rpc_method(gather=False)
     def load_training_state(self, input_dir: str) -> None:
-        path = Path(input_dir) / "training_state.pt"
+        path = Path(input_dir) / (f"training_state_rank{self.rank}.pt" if self.sharded
+                                  else "training_state.pt")
         state = torch.load(path, map_location=self.device, weights_only=False)
+        if self.sharded and state.get("world_size") != self.world_size:
+            raise ValueError(f"{path} was saved by {state.get('world_size')} ranks, "
+                             f"this job has {self.world_size}")
         self.optimizer.load_state_dict(state["optimizer"])
         self.lr_scheduler.load_state_dict(state["lr_scheduler"])
         self.step_count = int(state.get("step_count", 0))

@@ -38,6 +38,10 @@ class TrainingConfig(BaseModel):
     adam_beta2: float = 0.95
     adam_epsilon: float = 1e-8
     max_grad_norm: float = 1.0
+    # data parallelism: shard the fp32 master copy and AdamW moments of the trainable tensors
+    # over the ranks (gradients reduce-scattered, updated shards all-gathered), the optimizer
+    # state sharding of FSDP2 / ZeRO-2; the frozen base model stays replicated
+    shard_optimizer_state: bool = True
     lr_scheduler_type: LRSchedulerType = "constant_with_warmup"
     lr_warmup_steps: int = 20
     # DDIS / OPSM / entropy mask

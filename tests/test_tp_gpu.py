@@ -53,8 +53,7 @@ def _run_allreduce(rank, port, q):
             errs.append(((x.float() - xr.float()).abs().max().item(),
                          (xn.float() - nr).abs().max().item()))
         check_device_error()
-        dist.barrier()
-        ctx.close()
+        ctx.shutdown()
         q.put((rank, errs, ctx.fused_calls))
     finally:
         dist.destroy_process_group()
@@ -124,10 +123,8 @@ def _run_engine(rank, port, q):
             runner.stop_followers()
         else:
             res = runner.follow()
-        torch.cuda.synchronize()
         check_device_error()
-        dist.barrier()
-        ctx.close()
+        ctx.shutdown()
         q.put((rank, res))
     finally:
         dist.destroy_process_group()

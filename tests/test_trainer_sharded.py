@@ -1,0 +1,96 @@
+"""Data-parallel trainer with the sharded optimizer state (gradients reduce-scattered, AdamW on
+each rank's slice, updated slices all-gathered) against the replicated optimizer (one
+all-reduce), on two gloo ranks: same parameters after several steps, per-rank optimizer state
+holds only the rank's slice, and the per-rank training state round-trips."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _samples(vocab):
+    from agent_factory_3_b200.trainer.types import TrainingSample
+    rng = np.random.default_rng(10)
+    out = []
+    for i, n in enumerate([40, 56, 24, 48, 32, 16]):
+        comp = np.zeros(n, np.int32)
+        comp[n // 3:] = 1
+        out.append(TrainingSample(
+            sample_id=f"s{i}", input_ids=rng.integers(0, vocab, n).astype(np.int64),
+            completion_mask=comp, gen_logprobs=(comp * -6.9).astype(np.float32),
+            advantages=(comp * (1.0 if i % 2 else -1.0)).astype(np.float32),
+            seq_token_count=int(comp.sum()), prompt_sequence_count=2, prompt_id=f"g{i // 2}",
+            divisor=2.0))
+    return out
+
+
+def _run(rank, port, q, tmp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    try:
+        from agent_factory_3_b200.models.gpt_oss import GptOssConfig
+        from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
+        from agent_factory_3_b200.trainer.training_config import TrainingConfig
+        mcfg = GptOssConfig.tiny()
+        res = {}
+        for sharded in (False, True):
+            cfg = TrainingConfig(model_id="tiny", lora_r=4, lora_alpha=8,
+                                 lora_target_modules=["q_proj", "o_proj", "gate_up_proj", "down_proj"],
+                                 random_init_seed=0, use_routing_replay=False, lr_warmup_steps=0,
+                                 learning_rate=1e-2, max_capacity=256, pad_to_multiple_of_training=8,
+                                 shard_optimizer_state=sharded, gradient_checkpointing=False)
+            tr = ModelTrainer(cfg, model_config=mcfg, device="cpu")
+            if rank == 0:   # rank 0 drives, rank 1 serves the broadcast calls
+                for _ in range(3):
+                    tr.train_step(_samples(mcfg.vocab_size))
+                if sharded:
+                    tr.save_training_state(tmp)
+                    before = {k: v.clone() for k, v in tr.optimizer.state[tr.shard_param].items()}
+                    tr.reset_optimizer_state()
+                    tr.load_training_state(tmp)
+                    after = tr.optimizer.state[tr.shard_param]
+                    res["roundtrip"] = all(torch.equal(before[k], after[k]) for k in before)
+                tr.rpc_shutdown()
+            else:
+                tr.rpc_worker_loop()
+            flat = torch.cat([p.detach().reshape(-1) for p in tr.trainable])
+            n_state = sum(v.numel() for st in tr.optimizer.state.values() for v in st.values()
+                          if torch.is_tensor(v) and v.dim() > 0)
+            res[sharded] = (flat, n_state, tr.sharded)
+        q.put((rank, (res[False][0] - res[True][0]).abs().max().item(),
+               res[False][0].abs().max().item(), res[False][1], res[True][1], res[True][2],
+               res.get("roundtrip", True)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_optimizer_matches_replicated(tmp_path):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run, args=(r, port, q, str(tmp_path))) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, diff, scale, n_rep, n_shard, sharded, roundtrip in outs:
+        assert sharded
+        assert diff <= 1e-5 * max(1.0, scale), (diff, scale)
+        assert n_shard * 2 <= n_rep + 64          # each rank keeps ~half of the moments
+        assert roundtrip
+    assert (tmp_path / "training_state_rank0.pt").exists()
+    assert (tmp_path / "training_state_rank1.pt").exists()
