@@ -32,6 +32,9 @@ def main():
     ap.add_argument("--page-size", type=int, default=64)
     ap.add_argument("--max-prefill-tokens", type=int, default=16384)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--spec", choices=["none", "block", "ngram"], default="none",
+                    help="speculative decoding: block = 1-layer random-init block draft model")
+    ap.add_argument("--spec-block", type=int, default=8)
     a = ap.parse_args()
 
     from ..engine.scheduler import Engine, Request
@@ -62,9 +65,16 @@ def main():
         torch.cuda.empty_cache()
         tp = TPContext(None, cpu_group, dev, max_tokens=a.max_prefill_tokens + a.requests,
                        hidden=cfg.hidden_size)
+    drafter = None
+    if a.spec == "block":
+        from ..engine.spec import BlockDraftModel
+        drafter = BlockDraftModel.from_target(model, n_layers=1, block=a.spec_block, seed=a.seed + 1)
+    elif a.spec == "ngram":
+        from ..engine.spec import NgramDrafter
+        drafter = NgramDrafter(block=a.spec_block)
     eng = Engine(model, num_pages=a.requests * pages_per_req + 64, page_size=a.page_size,
                  max_running=a.requests, max_prefill_tokens=a.max_prefill_tokens, tp=tp,
-                 tp_shards=shards)
+                 tp_shards=shards, drafter=drafter)
     if rank != 0:
         eng.runner.follow()
         tp.shutdown()
@@ -132,6 +142,10 @@ def main():
         out["decode_step_ms"] = round(dec / max(1, a.gen - 1) * 1000, 2)
     if tp is not None:
         out["fused_allreduce_calls"] = tp.fused_calls
+    if drafter is not None:
+        out["spec"] = {"drafter": a.spec, "block": a.spec_block,
+                       "accept_length": round(eng.spec_accept_length, 3),
+                       "verifies": eng.spec_verifies}
     if err:
         out["device_error"] = err
     print(json.dumps(out), flush=True)

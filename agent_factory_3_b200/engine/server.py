@@ -211,22 +211,63 @@ def main():
     ap.add_argument("--lora-r", type=int, default=0, help="LoRA capacity (0 = no LoRA serving)")
     ap.add_argument("--lora-targets", default="q_proj,k_proj,v_proj,o_proj")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--speculative-algorithm", choices=["none", "block", "ngram"], default="none",
+                    help="block: one-forward block draft model sharing the target's embeddings")
+    ap.add_argument("--speculative-num-draft-tokens", type=int, default=8)
+    ap.add_argument("--speculative-draft-layers", type=int, default=1)
     a = ap.parse_args()
     from pathlib import Path
     p = Path(a.model)
     cfg = GptOssConfig.load(p / "config.json") if (p / "config.json").exists() else GptOssConfig.preset(a.model)
     lora = LoraConfig(r=a.lora_r, lora_alpha=2 * a.lora_r, target_modules=a.lora_targets.split(",")) if a.lora_r else None
-    model = GptOssForCausalLM(cfg, lora=lora, device="cuda")
+    import os
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:   # tensor parallel under torchrun: rank 0 serves HTTP, the others follow
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=1))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = GptOssForCausalLM(cfg, lora=lora if world == 1 else None, device=dev)
     if p.is_dir():
         load_checkpoint(p, model)
     else:
         model.init_random(a.seed)
     model.eval()
+    tp = shards = None
+    if world > 1:
+        from .tp import TPContext, broadcast_model, shard_model
+        broadcast_model(model)
+        shards = shard_model(model, rank, world, free_full=True)
+        torch.cuda.empty_cache()
+        tp = TPContext(None, cpu_group, dev, max_tokens=a.max_prefill_tokens + a.max_running_requests,
+                       hidden=cfg.hidden_size)
+    drafter = None
+    if a.speculative_algorithm == "block":
+        from .spec import BlockDraftModel
+        drafter = BlockDraftModel.from_target(model, n_layers=a.speculative_draft_layers,
+                                              block=a.speculative_num_draft_tokens, seed=a.seed + 1)
+    elif a.speculative_algorithm == "ngram":
+        from .spec import NgramDrafter
+        drafter = NgramDrafter(block=a.speculative_num_draft_tokens)
     eng = Engine(model, num_pages=a.num_pages, page_size=a.page_size,
-                 max_running=a.max_running_requests, max_prefill_tokens=a.max_prefill_tokens).start()
-    web.run_app(build_app(eng, {"model": a.model, "num_hidden_layers": cfg.num_hidden_layers,
-                                "num_experts_per_tok": cfg.num_experts_per_tok}),
-                host=a.host, port=a.port)
+                 max_running=a.max_running_requests, max_prefill_tokens=a.max_prefill_tokens,
+                 tp=tp, tp_shards=shards, drafter=drafter)
+    if rank != 0:
+        eng.runner.follow()
+        tp.shutdown()
+        return
+    eng.start()
+    try:
+        web.run_app(build_app(eng, {"model": a.model, "num_hidden_layers": cfg.num_hidden_layers,
+                                    "num_experts_per_tok": cfg.num_experts_per_tok}),
+                    host=a.host, port=a.port)
+    finally:
+        eng.stop()
+        if tp is not None:
+            tp.shutdown()
     torch.cuda.synchronize()
 
 

@@ -7,8 +7,8 @@ buffer: a 256-byte flag area (one uint32 arrival epoch per rank) followed by ``s
 equally-sized data sets that alternate between successive collective calls.
 
 The reference has no such layer: its rollout engine (sglang) reduces with NCCL or its own
-custom all-reduce, and its trainer uses NCCL only.  No multicast object is created (plain peer
-mappings), so a rank that exits cannot fault the others through an NVLink multicast binding.
+custom all-reduce, and its trainer uses NCCL only.  Only plain peer mappings are made (no NVLS
+switch-memory binding), so a rank that exits cannot fault the others through such a binding.
 """
 from __future__ import annotations
 
