@@ -114,7 +114,8 @@ def main():
     reqs = []
     for i in range(a.requests):
         r = Request(input_ids=torch.randint(0, cfg.vocab_size, (a.prompt,), generator=g).tolist(),
-                    max_new_tokens=a.gen, temperature=1.0, seed=i, stop_token_ids=[])
+                    max_new_tokens=a.gen, temperature=1.0, seed=i, stop_token_ids=[],
+                    stream=True)   # per-step callbacks: the first token of each request is seen
         r.on_output = make_cb(r)
         reqs.append(r)
     t_start = time.perf_counter()

@@ -51,6 +51,7 @@ class Request:
     extra_key: Optional[str] = None
     stream: bool = False
     on_output: Optional[Callable[[dict], None]] = None   # called from the engine thread
+    abort_after_tokens: Optional[int] = None   # injected fault: abort once this many are out
     rid: int = field(default_factory=lambda: next(_ids))
     # state
     output_ids: list[int] = field(default_factory=list)
@@ -344,6 +345,8 @@ class Engine:
         r.output_entropy.append(float(ent))
         if r.stop_token_ids and t in r.stop_token_ids:
             r.finish_reason = {"type": "stop", "matched": int(t)}
+        elif r.abort_after_tokens is not None and len(r.output_ids) >= r.abort_after_tokens:
+            r.finish_reason = {"type": "abort", "message": "injected fault"}
         elif len(r.output_ids) >= r.max_new_tokens:
             r.finish_reason = {"type": "length"}
         elif len(r.all_ids) >= self.max_context:

@@ -53,8 +53,13 @@ def _request_from_json(body: dict) -> Request:
         stream=bool(body.get("stream", False)))
 
 
-def build_app(engine: Engine, model_info: dict | None = None) -> web.Application:
+def build_app(engine: Engine, model_info: dict | None = None, faults=None) -> web.Application:
+    """``faults``: an ``engine.faults.FaultPlan`` (default: from AF3_ENGINE_FAULTS) that makes
+    /generate drop, delay or abort requests on purpose, for client robustness tests."""
     app = web.Application(client_max_size=1 << 30)
+    if faults is None:
+        from .faults import FaultPlan
+        faults = FaultPlan.from_env()
 
     async def generate(request: web.Request):
         body = await request.json()
@@ -63,6 +68,15 @@ def build_app(engine: Engine, model_info: dict | None = None) -> web.Application
         if min(req.input_ids) < 0 or max(req.input_ids) >= vocab:
             # never let an out-of-range id reach the embedding gather on the device
             return web.json_response({"error": f"input_ids must lie in [0, {vocab})"}, status=400)
+        abort_at = None
+        if faults is not None:
+            if faults.delay_ms > 0:
+                await asyncio.sleep(faults.delay_ms / 1000.0)
+            if faults.should_drop():
+                return web.json_response({"error": "injected fault: request dropped"}, status=503)
+            abort_at = faults.abort_point()
+            faults.aborted += int(abort_at is not None)
+        req.abort_after_tokens = abort_at
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         req.on_output = lambda out: loop.call_soon_threadsafe(q.put_nowait, out)

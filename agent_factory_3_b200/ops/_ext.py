@@ -19,8 +19,13 @@ _LAUNCHES_PER_CALL = {"moe_group": 4, "attn_bwd": 3, "decode_attention": 2, "dev
 _launch_count = 0
 
 
+_NVTX = os.environ.get("AF3_NVTX") == "1"
+
+
 class _CountingExt:
-    """Proxy of the extension module that counts the kernels its entry points launch."""
+    """Proxy of the extension module that counts the kernels its entry points launch.  With
+    AF3_NVTX=1 every entry point also runs inside an NVTX range named ``af3.<entry point>``,
+    so a timeline profiler shows which native op issued each kernel."""
 
     def __init__(self, mod):
         self._mod = mod
@@ -30,6 +35,17 @@ class _CountingExt:
         if not callable(fn):
             return fn
         n = _LAUNCHES_PER_CALL.get(name, 1)
+
+        if _NVTX:
+            def call(*a, **k):
+                global _launch_count
+                _launch_count += n
+                torch.cuda.nvtx.range_push(f"af3.{name}")
+                try:
+                    return fn(*a, **k)
+                finally:
+                    torch.cuda.nvtx.range_pop()
+            return call
 
         def call(*a, **k):
             global _launch_count
