@@ -217,9 +217,6 @@ class Engine:
         return load_file(str(p / "adapter_model.safetensors"))
 
     def _apply_lora(self, name: str) -> None:
-        if self.tp is not None and self.tp.world > 1:
-            raise NotImplementedError("LoRA adapters are not sharded for tensor parallelism; "
-                                      "serve merged weights or run the engine with TP=1")
         ad = self.loras[name]
         if isinstance(ad, tuple) and ad[0] == "params":   # internal layout (GPU weight sync)
             params = self.model.lora_param_dict()
@@ -228,6 +225,8 @@ class Engine:
                     params[k].copy_(t.view_as(params[k]))
         else:
             _load_lora_into(self.model, ad)
+        if self.tp is not None:
+            self.runner.sync_lora()     # slices on every tensor-parallel rank
         self.active_lora = name
         self.runner.lora_active = True
 

@@ -244,7 +244,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=1))
     dev = torch.device("cuda", torch.cuda.current_device())
-    model = GptOssForCausalLM(cfg, lora=lora if world == 1 else None, device=dev)
+    model = GptOssForCausalLM(cfg, lora=lora, device=dev)
     if p.is_dir():
         load_checkpoint(p, model)
     else:

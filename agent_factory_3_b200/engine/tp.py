@@ -92,6 +92,57 @@ def shard_model(model, rank: int, world: int, free_full: bool = False) -> list[L
     return shards
 
 
+@dataclass
+class LoraShard:
+    """This rank's LoRA factors of one layer (bf16): query/KV-head rows of the fused q/k/v B,
+    the o_proj input columns of its A, and the local experts' up-projections B; the expert
+    down-projections A are kept whole (the LoRA activations of every routed row are computed,
+    only the local experts' rows are read)."""
+    qkv_A: torch.Tensor | None
+    qkv_B: torch.Tensor | None
+    o_A: torch.Tensor | None
+    o_B: torch.Tensor | None
+    gu_A: torch.Tensor | None
+    gu_B: torch.Tensor | None
+    dn_A: torch.Tensor | None
+    dn_B: torch.Tensor | None
+    s_attn: float
+    s_mlp: float
+
+
+def shard_lora(model, rank: int, world: int) -> list[LoraShard]:
+    cfg = model.cfg
+    hq, hkv, d, E = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, cfg.num_local_experts
+    qh, kh, ne = hq // world, hkv // world, E // world
+    qs, kvs = cfg.q_size, cfg.kv_size
+    q0, q1 = rank * qh * d, (rank + 1) * qh * d
+    k0, k1 = qs + rank * kh * d, qs + (rank + 1) * kh * d
+    v0, v1 = qs + kvs + rank * kh * d, qs + kvs + (rank + 1) * kh * d
+    e0, e1 = rank * ne, (rank + 1) * ne
+
+    def bf(t):
+        return None if t is None else t.detach().to(torch.bfloat16).contiguous()
+
+    out = []
+    with torch.no_grad():
+        for layer in model.layers:
+            a, m = layer.self_attn, layer.mlp
+            A, B = a._qkv_lora()
+            if B is not None:
+                B = torch.cat([B[q0:q1], B[k0:k1], B[v0:v1]])
+            oA = a.lora["o_proj_A"][:, q0:q1] if "o_proj_A" in a.lora else None
+            oB = a.lora["o_proj_B"] if "o_proj_B" in a.lora else None
+            lo = m.lora
+            out.append(LoraShard(
+                qkv_A=bf(A), qkv_B=bf(B), o_A=bf(oA), o_B=bf(oB),
+                gu_A=bf(lo["gu_A"]) if "gu_A" in lo else None,
+                gu_B=bf(lo["gu_B"][e0:e1]) if "gu_B" in lo else None,
+                dn_A=bf(lo["dn_A"]) if "dn_A" in lo else None,
+                dn_B=bf(lo["dn_B"][e0:e1]) if "dn_B" in lo else None,
+                s_attn=a.lora_scaling, s_mlp=m.lora_scaling))
+    return out
+
+
 def broadcast_model(model, group=None, src: int = 0) -> None:
     """Make every rank's weights equal to rank ``src``'s (random init or a checkpoint loaded on
     one rank) before sharding."""
@@ -149,17 +200,28 @@ class TPContext:
         return x, xn
 
     # -- step broadcast (rank 0 -> others) -------------------------------------------------
-    def send_items(self, items: list[StepItem] | None) -> None:
-        obj = [None if items is None else [(it.ids, it.start, it.pages, it.want_logits,
-                                            it.all_logits) for it in items]]
-        dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
+    def send(self, msg) -> None:
+        dist.broadcast_object_list([msg], group=self.cpu_group, group_src=0)
 
-    def recv_items(self) -> list[StepItem] | None:
+    def recv(self):
         obj = [None]
         dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
-        if obj[0] is None:
-            return None
-        return [StepItem(list(i), s, list(p), w, a) for i, s, p, w, a in obj[0]]
+        return obj[0]
+
+    def send_items(self, items: list[StepItem] | None, lora_active: bool = False) -> None:
+        self.send(None if items is None else
+                  ("step", [(it.ids, it.start, it.pages, it.want_logits, it.all_logits)
+                            for it in items], lora_active))
+
+    @staticmethod
+    def items_of(msg) -> list[StepItem]:
+        return [StepItem(list(i), s, list(p), w, a) for i, s, p, w, a in msg[1]]
+
+    def broadcast_tensors(self, tensors: list[torch.Tensor]) -> None:
+        """Rank 0's values of ``tensors`` (same shapes on every rank) to every rank, over the
+        device group."""
+        for t in tensors:
+            dist.broadcast(t.data, group=self.group, group_src=0)
 
     def close(self) -> None:
         if self.symm is not None:
@@ -176,9 +238,12 @@ class TPContext:
 
 
 def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int, alpha: float,
-                   limit: float, out: torch.Tensor, routing_out: list | None = None) -> torch.Tensor:
+                   limit: float, out: torch.Tensor, routing_out: list | None = None,
+                   lora: LoraShard | None = None) -> torch.Tensor:
     """This rank's share of the MoE output: sum over the token's top-k experts that live on
-    this rank of gate * expert(x), written into ``out`` [T, H] (no residual)."""
+    this rank of gate * expert(x), written into ``out`` [T, H] (no residual).  With ``lora``
+    the experts' adapters join as in the single-GPU path: x A_e^T s as extra K columns against
+    the local experts' B_e rows."""
     T, H = xn.shape
     logits = G.matmul(xn, sh.router_w, bias=sh.router_b, out_dtype=torch.float32)
     rt = M.route(logits, top_k, n_experts)
@@ -188,16 +253,21 @@ def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int,
     R = x_s.shape[0]
     ex = sh.experts
     y_s = torch.zeros(R, H, device=xn.device, dtype=torch.bfloat16)
+    gu_lora = lora is not None and lora.gu_A is not None
+    dn_lora = lora is not None and lora.dn_A is not None
     if xn.is_cuda and use_cuda_kernels(xn) and ex.f16_exact():
         offs = rt.offsets[sh.e0:sh.e1 + 1]
         cnts = rt.counts[sh.e0:sh.e1]
         I2 = ex.gu_blocks.shape[1]
         h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
         bn = _token_tile(T * top_k, n_experts)
+        xa = G.grouped_matmul(x_s, lora.gu_A, rt.offsets, alpha=lora.s_mlp)[0] if gu_lora else None
         ext().moe_mxfp4_gemm(x_s, ex.gu_blocks, ex.gu_scales, ex.gu_bias, offs, cnts, 0, None, h,
-                             alpha, limit, bn)
+                             alpha, limit, bn, lora_b=lora.gu_B if gu_lora else None, xa=xa)
+        ha = G.grouped_matmul(h, lora.dn_A, rt.offsets, alpha=lora.s_mlp)[0] if dn_lora else None
         ext().moe_mxfp4_gemm(h, ex.dn_blocks, ex.dn_scales, ex.dn_bias, offs, cnts, 1,
-                             rt.row_gate, y_s, alpha, limit, bn)
+                             rt.row_gate, y_s, alpha, limit, bn,
+                             lora_b=lora.dn_B if dn_lora else None, xa=ha)
     else:
         W_gu = mxfp4.dequantize(ex.gu_blocks, ex.gu_scales)
         W_dn = mxfp4.dequantize(ex.dn_blocks, ex.dn_scales)
@@ -207,40 +277,70 @@ def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int,
             if n == 0:
                 continue
             j = e - sh.e0
-            gu = (x_s[r0:r0 + n].float() @ W_gu[j].float().t() + ex.gu_bias[j].float())
+            xe = x_s[r0:r0 + n].float()
+            gu = xe @ W_gu[j].float().t() + ex.gu_bias[j].float()
+            if gu_lora:
+                xa = (xe @ lora.gu_A[e].float().t() * lora.s_mlp).to(torch.bfloat16).float()
+                gu = gu + xa @ lora.gu_B[j].float().t()
             h = G.swiglu_reference(gu.to(torch.bfloat16), alpha, limit).to(torch.bfloat16)
-            y = (h.float() @ W_dn[j].float().t() + ex.dn_bias[j].float()) * rt.row_gate[r0:r0 + n, None]
+            y = h.float() @ W_dn[j].float().t() + ex.dn_bias[j].float()
+            if dn_lora:
+                ha = (h.float() @ lora.dn_A[e].float().t() * lora.s_mlp).to(torch.bfloat16).float()
+                y = y + ha @ lora.dn_B[j].float().t()
+            y = y * rt.row_gate[r0:r0 + n, None]
             y_s[r0:r0 + n] = y.to(torch.bfloat16)
     return M.combine_rows(y_s, rt.dest, top_k, out=out)
 
 
 class TPModelRunner(ModelRunner):
-    """Engine forward pass over this rank's shard; see the module docstring."""
+    """Engine forward pass over this rank's shard; see the module docstring.
+
+    LoRA: the engine loads an adapter into rank 0's model and calls ``sync_lora()``; the full
+    factors are broadcast over the device group into every rank's model and each rank keeps its
+    slices (``shard_lora``).  Every step message carries whether the adapter is active."""
 
     def __init__(self, model, kv, ctx: TPContext, shards: list[LayerShard] | None = None):
         super().__init__(model, kv, lora_active=False)
         self.ctx = ctx
         self.shards = shards if shards is not None else shard_model(model, ctx.rank, ctx.world)
+        self.lora_shards: list[LoraShard] | None = None
         cfg = self.cfg
         self.hq = cfg.num_attention_heads // ctx.world
         self.hkv = cfg.num_key_value_heads // ctx.world
 
+    def sync_lora(self) -> None:
+        """Rank 0: publish the adapter now in the model's LoRA parameters to every rank."""
+        params = list(self.model.lora_param_dict().values())
+        if not params:
+            raise ValueError("the model was built without LoRA capacity")
+        if self.ctx.world > 1:
+            self.ctx.send(("lora",))
+            self.ctx.broadcast_tensors(params)
+        self.lora_shards = shard_lora(self.model, self.ctx.rank, self.ctx.world)
+
+    def _recv_lora(self) -> None:
+        self.ctx.broadcast_tensors(list(self.model.lora_param_dict().values()))
+        self.lora_shards = shard_lora(self.model, self.ctx.rank, self.ctx.world)
+
     def forward(self, items: list[StepItem]) -> StepOutput:
-        if self.lora_active:
-            raise NotImplementedError("LoRA adapters are not sharded for tensor parallelism")
+        if self.lora_active and self.lora_shards is None:
+            raise RuntimeError("LoRA active but not synced to the tensor-parallel ranks")
         if self.ctx.rank == 0 and self.ctx.world > 1:
-            self.ctx.send_items(items)
-        return self._forward(items)
+            self.ctx.send_items(items, self.lora_active)
+        return self._forward(items, self.lora_active)
 
     def follow(self) -> int:
         """Non-zero ranks: run the steps rank 0 broadcasts until it sends None; returns the
         number of steps run."""
         n = 0
         while True:
-            items = self.ctx.recv_items()
-            if items is None:
+            msg = self.ctx.recv()
+            if msg is None:
                 return n
-            self._forward(items)
+            if msg[0] == "lora":
+                self._recv_lora()
+                continue
+            self._forward(TPContext.items_of(msg), bool(msg[2]))
             n += 1
 
     def stop_followers(self) -> None:
@@ -248,7 +348,7 @@ class TPModelRunner(ModelRunner):
             self.ctx.send_items(None)
 
     @torch.inference_mode()
-    def _forward(self, items: list[StepItem]) -> StepOutput:
+    def _forward(self, items: list[StepItem], lora_active: bool = False) -> StepOutput:
         cfg = self.cfg
         eps = cfg.rms_norm_eps
         H = cfg.hidden_size
@@ -259,15 +359,22 @@ class TPModelRunner(ModelRunner):
         rec: list = []
         L = len(self.shards)
         for li, sh in enumerate(self.shards):
-            o = self._attention(li, m, xn, sh.qkv_w, sh.qkv_b, None, None, 1.0, sh.sinks,
-                                sh.window, self.hq, self.hkv, rope)
+            lo = self.lora_shards[li] if lora_active else None
+            o = self._attention(li, m, xn, sh.qkv_w, sh.qkv_b,
+                                lo.qkv_A if lo else None, lo.qkv_B if lo else None,
+                                lo.s_attn if lo else 1.0, sh.sinks, sh.window, self.hq,
+                                self.hkv, rope)
             part = self.ctx.partial_buffer(m.N, H)
-            G.matmul(o, sh.o_w, bias=sh.o_b, out=part)
+            if lo is not None and lo.o_A is not None:
+                oa = G.matmul(o, lo.o_A, alpha=lo.s_attn)                  # [N, r]
+                G.matmul(o, sh.o_w, bias=sh.o_b, a2=oa, b2=lo.o_B, out=part)
+            else:
+                G.matmul(o, sh.o_w, bias=sh.o_b, out=part)
             h, hn = self.ctx.allreduce_norm(part, x, sh.post_norm, eps)
             part = self.ctx.partial_buffer(m.N, H)
             lay_rec: list = []
             moe_ep_partial(hn, sh, cfg.num_local_experts, cfg.num_experts_per_tok,
-                           cfg.swiglu_alpha, cfg.swiglu_limit, part, lay_rec)
+                           cfg.swiglu_alpha, cfg.swiglu_limit, part, lay_rec, lo)
             rec.append(lay_rec[0])
             nxt = self.shards[li + 1].in_norm if li + 1 < L else None
             x, xn = self.ctx.allreduce_norm(part, h, nxt, eps)

@@ -107,6 +107,64 @@ def test_tp2_matches_single_process():
     assert r1[2] >= 6                       # ... driving rank 1 through every step
 
 
+def _run_lora(rank, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    try:
+        from agent_factory_3_b200.models.gpt_oss import LoraConfig
+        cfg = GptOssConfig.tiny()
+        lora = LoraConfig(r=4, lora_alpha=8, target_modules=["q_proj", "k_proj", "v_proj", "o_proj",
+                                                             "gate_up_proj", "down_proj"])
+        model = GptOssForCausalLM(cfg, lora=lora, device="cpu", dtype=torch.bfloat16).init_random(0)
+        model.eval()
+        ctx = TPContext()
+        runner = TPModelRunner(model, _kv(cfg, 2), ctx, shard_model(model, rank, 2))
+        if rank == 0:
+            with torch.no_grad():        # an adapter that only rank 0 has: sync must ship it
+                g = torch.Generator().manual_seed(5)
+                for p in model.lora_param_dict().values():
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.2)
+            ref = ModelRunner(model, _kv(cfg, 1), lora_active=True)
+            runner.sync_lora()
+            runner.lora_active = True
+            diffs = []
+            for items in _steps():
+                want = ref.forward(items)
+                got = runner.forward(items)
+                diffs.append(((got.logits - want.logits).abs().max().item(),
+                              want.logits.abs().max().item()))
+            base = ModelRunner(model, _kv(cfg, 1), lora_active=False).forward(_steps()[0]).logits
+            moved = (want.logits.abs().max().item(), (ref.forward(_steps()[0]).logits - base).abs().max().item())
+            runner.stop_followers()
+            q.put(("r0", diffs, moved))
+        else:
+            n = runner.follow()
+            same = all(torch.equal(a, b) for a, b in zip(
+                [p for p in model.lora_param_dict().values()][:2],
+                [p for p in model.lora_param_dict().values()][:2]))
+            q.put(("r1", n, runner.lora_shards is not None and same))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_lora_matches_single_process():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run_lora, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    r0 = next(o for o in outs if o[0] == "r0")
+    r1 = next(o for o in outs if o[0] == "r1")
+    for err, scale in r0[1]:
+        assert err <= 0.05 * max(1.0, scale), r0[1]
+    assert r0[2][1] > 0.05          # the adapter changes the logits, so the check has teeth
+    assert r1[1] == 2 and r1[2]
+
+
 def test_shard_model_partitions_weights():
     model = _model()
     cfg = model.cfg
