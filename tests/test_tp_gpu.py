@@ -92,13 +92,15 @@ def _run_engine(rank, port, q):
         from agent_factory_3_b200.engine.model_runner import ModelRunner, StepItem
         from agent_factory_3_b200.engine.tp import (TPContext, TPModelRunner, broadcast_model,
                                                     shard_model)
-        from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM
+        from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
         from agent_factory_3_b200.ops._ext import check_device_error
         dev = torch.device("cuda", rank)
         cfg = GptOssConfig.preset("gpt-oss-20b")
         cfg.num_hidden_layers = 2
         cfg.layer_types = cfg.layer_types[:2]
-        model = GptOssForCausalLM(cfg, device=dev).init_random(0).eval()
+        lora = LoraConfig(r=16, lora_alpha=32, target_modules=["q_proj", "k_proj", "v_proj", "o_proj",
+                                                               "gate_up_proj", "down_proj"])
+        model = GptOssForCausalLM(cfg, lora=lora, device=dev).init_random(0).eval()
         broadcast_model(model)
 
         def kv(world):
@@ -113,13 +115,22 @@ def _run_engine(rank, port, q):
         ctx = TPContext(None, cpu, dev, max_tokens=256, hidden=cfg.hidden_size)
         runner = TPModelRunner(model, kv(2), ctx, shard_model(model, rank, 2))
         if rank == 0:
-            ref = ModelRunner(model, kv(1), lora_active=False)
             res = []
-            for items in steps:
-                want = ref.forward(items).logits
-                got = runner.forward(items).logits
-                res.append(((got - want).abs().max().item(), want.abs().max().item(),
-                            float((got.argmax(-1) == want.argmax(-1)).float().mean())))
+            for active in (False, True):
+                if active:     # an adapter only rank 0 holds; sync_lora ships it
+                    with torch.no_grad():
+                        gg = torch.Generator(device=dev).manual_seed(11)
+                        for p in model.lora_param_dict().values():
+                            p.copy_(torch.randn(p.shape, generator=gg, device=dev) * 0.05)
+                    runner.sync_lora()
+                runner.lora_active = active
+                ref = ModelRunner(model, kv(1), lora_active=active)
+                for items in steps:
+                    want = ref.forward(items).logits
+                    got = runner.forward(items).logits
+                    res.append(((got - want).abs().max().item(), want.abs().max().item(),
+                                float((got.argmax(-1) == want.argmax(-1)).float().mean())))
+                # the second pass rewrites the same KV slots (same pages), so no reset is needed
             runner.stop_followers()
         else:
             res = runner.follow()
@@ -141,6 +152,7 @@ def test_tp2_runner_matches_single_gpu():
     outs = dict(q.get(timeout=600) for _ in range(2))
     for p in ps:
         p.join(timeout=60)
-    assert outs[1] == 2
+    assert outs[1] == 4
+    assert len(outs[0]) == 4
     for err, scale, agree in outs[0]:
         assert err <= 0.05 * max(1.0, scale), outs[0]
