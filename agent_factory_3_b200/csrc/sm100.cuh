@@ -81,6 +81,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase completes or `ns`
+// nanoseconds pass, so waiting warps stop taking issue slots from the working warps.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred P;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n"
+      "selp.b32 %0, 1, 0, P;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -94,15 +110,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
                                           volatile int* abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (abort_flag && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > (uint64_t)AF3_WAIT_NS) {
-        if (err) atomicExch(err, kErrMbarTimeout);
-        if (abort_flag) *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    // suspended until the phase flips (or 20 us pass), then the bounds are checked
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+    if (abort_flag && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > (uint64_t)AF3_WAIT_NS) {
+      if (err) atomicExch(err, kErrMbarTimeout);
+      if (abort_flag) *abort_flag = 1;
+      return false;
     }
   }
 }

@@ -76,20 +76,31 @@ class ModelRunner:
                 pos.append(p)
                 slots.append(it.pages[p // P] * P + p % P)
             rows.append((r0, r0 + n))
-            (dec_idx if (n == 1 and it.start > 0) else pre_idx).append(i)
+            # a speculative verify block on top of cached pages is decoded row by row: its K/V
+            # are stored first, so token j attends to start + j + 1 cached positions
+            decode = it.start > 0 and (n == 1 or it.all_logits)
+            (dec_idx if decode else pre_idx).append(i)
         m.N, m.rows, m.dec_idx, m.pre_idx = len(ids), rows, dec_idx, pre_idx
         m.ids_t = torch.tensor(ids, device=dev, dtype=torch.long)
         m.pos_t = torch.tensor(pos, device=dev, dtype=torch.int32)
         m.slots_t = torch.tensor(slots, device=dev, dtype=torch.int32)
         if dec_idx:
             maxp = max(len(items[i].pages) for i in dec_idx)
-            pt = torch.zeros(len(dec_idx), maxp, dtype=torch.int32)
-            for r, i in enumerate(dec_idx):
-                pt[r, :len(items[i].pages)] = torch.tensor(items[i].pages, dtype=torch.int32)
+            n_dec = sum(len(items[i].ids) for i in dec_idx)
+            pt = torch.zeros(n_dec, maxp, dtype=torch.int32)
+            lens, drows, r = [], [], 0
+            for i in dec_idx:
+                it = items[i]
+                pg = torch.tensor(it.pages, dtype=torch.int32)
+                for j in range(len(it.ids)):
+                    pt[r, :len(it.pages)] = pg
+                    lens.append(it.start + j + 1)
+                    drows.append(rows[i][0] + j)
+                    r += 1
             m.dec_pt = pt.to(dev)
-            m.dec_lens = torch.tensor([items[i].start + 1 for i in dec_idx], device=dev, dtype=torch.int32)
-            m.dec_rows = torch.tensor([rows[i][0] for i in dec_idx], device=dev, dtype=torch.long)
-            m.dec_max = int(max(items[i].start + 1 for i in dec_idx))
+            m.dec_lens = torch.tensor(lens, device=dev, dtype=torch.int32)
+            m.dec_rows = torch.tensor(drows, device=dev, dtype=torch.long)
+            m.dec_max = int(max(lens))
         if pre_idx:   # packed full contexts of the prefill chunks
             ctx_slots, new_in_ctx, new_rows, tiles, cu = [], [], [], [], [0]
             for i in pre_idx:
