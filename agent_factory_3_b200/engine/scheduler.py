@@ -424,19 +424,17 @@ class Engine:
                 if r.stream and r.finish_reason is None:
                     self._emit(r, final=False)
         if spec_reqs:
-            from .spec import verify_block
+            from .spec import verify_batch
+            idx = [n_plain + j for j in range(len(spec_reqs))]
+            g = None
+            if any(r.temperature > 0 for r in spec_reqs):
+                g = torch.Generator(device=out.logits.device)
+                g.manual_seed((self.step_count * 1000003 + sum(r.rid for r in spec_reqs)) % (2 ** 63))
+            results = verify_batch(out.logits, [out.logit_offsets[i] for i in idx],
+                                   [items[i].ids[1:] for i in idx],
+                                   [r.temperature for r in spec_reqs], g)
             n_new = 0
-            for j, r in enumerate(spec_reqs):
-                i = n_plain + j
-                o = out.logit_offsets[i]
-                it = items[i]
-                g = None
-                if r.temperature > 0:
-                    g = torch.Generator(device=out.logits.device)
-                    g.manual_seed(((r.seed if r.seed is not None else r.rid) * 1000003
-                                   + len(r.output_ids)) % (2 ** 63))
-                a, toks, lps, ents = verify_block(out.logits[o:o + len(it.ids)], it.ids[1:],
-                                                  r.temperature, g)
+            for r, (a, toks, lps, ents) in zip(spec_reqs, results):
                 r.n_cached += a + 1          # the last token and the accepted drafts now have KV
                 self.spec_verifies += 1
                 self.spec_accepted += a

@@ -145,3 +145,80 @@ def verify_block(logits: torch.Tensor, drafts: list[int], temperature: float,
     lps = logp[idx, sel].tolist()
     ents = (-(logp[:len(toks)].exp() * logp[:len(toks)]).sum(-1)).tolist()
     return a, toks, lps, ents
+
+
+def verify_batch(logits: torch.Tensor, offsets: list[int], drafts: list[list[int]],
+                 temperatures: list[float], generator: torch.Generator | None = None):
+    """``verify_block`` for every request of a step at once: request i's block occupies logits
+    rows offsets[i] .. offsets[i] + len(drafts[i]).  Same acceptance rules; the work stays on
+    the device and crosses to the host three times per step (not per request)."""
+    dev = logits.device
+    lg = logits.float()
+    rows_t, draft_rows, draft_tok = [], [], []
+    for o, d, t in zip(offsets, drafts, temperatures):
+        rows_t += [t] * (len(d) + 1)
+        draft_rows += list(range(o, o + len(d)))
+        draft_tok += list(d)
+    # per-row temperature over the rows the blocks occupy (absolute row indices)
+    all_rows = []
+    for o, d in zip(offsets, drafts):
+        all_rows += list(range(o, o + len(d) + 1))
+    ar = torch.tensor(all_rows, device=dev, dtype=torch.long)
+    temp_rows = torch.ones(lg.shape[0], device=dev, dtype=torch.float32)
+    temp_rows[ar] = torch.tensor(rows_t, device=dev, dtype=torch.float32)
+    scaled = torch.where(temp_rows[:, None] > 0, lg / temp_rows.clamp_min(1e-6)[:, None], lg)
+    logp = torch.log_softmax(scaled, -1)
+    pred = lg.argmax(-1)
+    if draft_rows:
+        dr = torch.tensor(draft_rows, device=dev, dtype=torch.long)
+        dt = torch.tensor(draft_tok, device=dev, dtype=torch.long)
+        p_d = logp[dr, dt].exp()
+        u = torch.rand(len(draft_rows), device=dev, generator=generator)
+        host = torch.stack([pred[dr].float(), p_d, u]).tolist()          # transfer 1
+    else:
+        host = [[], [], []]
+    # acceptance on the host
+    res, k = [], 0
+    need_rows, need_excl = [], []
+    for i, (o, d, t) in enumerate(zip(offsets, drafts, temperatures)):
+        a = 0
+        while a < len(d):
+            j = k + a
+            ok = (int(host[0][j]) == d[a]) if t <= 0 else (host[2][j] < host[1][j])
+            if not ok:
+                break
+            a += 1
+        k += len(d)
+        res.append([a, o, t, d])
+        need_rows.append(o + a)
+        need_excl.append(d[a] if (a < len(d) and t > 0) else -1)
+    # the token after the accepted prefix: greedy pick, or a sample (draft removed on rejection)
+    nr = torch.tensor(need_rows, device=dev, dtype=torch.long)
+    probs = logp[nr].exp()
+    excl = torch.tensor(need_excl, device=dev, dtype=torch.long)
+    has = excl >= 0
+    if bool(has.any()):
+        probs[has.nonzero().squeeze(1), excl[has]] = 0.0
+    sampled = torch.multinomial(probs / probs.sum(-1, keepdim=True).clamp_min(1e-30), 1,
+                                generator=generator).squeeze(1)
+    greedy_next = pred[nr]
+    is_greedy = torch.tensor([t <= 0 for _, _, t, _ in res], device=dev)
+    nxt = torch.where(is_greedy, greedy_next, sampled).tolist()              # transfer 2
+    # log-probs and entropies of every emitted token
+    em_rows, em_tok = [], []
+    for (a, o, t, d), x in zip(res, nxt):
+        toks = d[:a] + [int(x)]
+        em_rows += list(range(o, o + len(toks)))
+        em_tok += toks
+    er = torch.tensor(em_rows, device=dev, dtype=torch.long)
+    et = torch.tensor(em_tok, device=dev, dtype=torch.long)
+    lp_rows = logp[er]
+    lps = lp_rows.gather(1, et[:, None]).squeeze(1)
+    ents = -(lp_rows.exp() * lp_rows).sum(-1)
+    lps_h, ents_h = torch.stack([lps, ents]).tolist()                          # transfer 3
+    out, q = [], 0
+    for (a, o, t, d), x in zip(res, nxt):
+        n = a + 1
+        out.append((a, d[:a] + [int(x)], lps_h[q:q + n], ents_h[q:q + n]))
+        q += n
+    return out

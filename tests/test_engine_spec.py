@@ -6,7 +6,8 @@ import threading
 import torch
 
 from agent_factory_3_b200.engine.scheduler import Engine, Request
-from agent_factory_3_b200.engine.spec import BlockDraftModel, NgramDrafter, verify_block
+from agent_factory_3_b200.engine.spec import (BlockDraftModel, NgramDrafter, verify_batch,
+                                              verify_block)
 from tests.test_engine import assert_greedy, tiny_model
 
 
@@ -39,6 +40,29 @@ def test_verify_block_greedy():
     assert a == 3 and toks == [3, 4, 7, 1]
     a, toks, _, _ = verify_block(lg, [0, 4, 7], 0.0)
     assert a == 0 and toks == [3]
+
+
+def test_verify_batch_matches_per_request():
+    torch.manual_seed(3)
+    lg = torch.randn(12, 9) * 3
+    drafts = [[int(lg[0].argmax()), 1], [int(lg[3].argmax()), int(lg[4].argmax()), 2], [5]]
+    offs = [0, 3, 7]
+    got = verify_batch(lg, offs, drafts, [0.0, 0.0, 0.0])
+    for (a, toks, lps, ents), o, d in zip(got, offs, drafts):
+        ra, rt, rl, re = verify_block(lg[o:o + len(d) + 1], d, 0.0)
+        assert (a, toks) == (ra, rt)
+        assert torch.allclose(torch.tensor(lps), torch.tensor(rl), atol=1e-5)
+        assert torch.allclose(torch.tensor(ents), torch.tensor(re), atol=1e-4)
+    # sampling: the first emitted token of a block follows the target distribution
+    T = 0.7
+    p = torch.softmax(lg[3] / T, -1)
+    counts = torch.zeros(9)
+    g = torch.Generator().manual_seed(2)
+    n = 6000
+    for _ in range(n):
+        res = verify_batch(lg, offs, drafts, [T, T, T], g)
+        counts[res[1][1][0]] += 1
+    assert (counts / n - p).abs().max() < 0.025
 
 
 def test_verify_block_sampling_matches_target():
