@@ -35,6 +35,7 @@ def main():
     ap.add_argument("--spec", choices=["none", "block", "ngram"], default="none",
                     help="speculative decoding: block = 1-layer random-init block draft model")
     ap.add_argument("--spec-block", type=int, default=8)
+    ap.add_argument("--cuda-graphs", action="store_true", help="replay decode steps from CUDA graphs (TP=1)")
     a = ap.parse_args()
 
     from ..engine.scheduler import Engine, Request
@@ -74,7 +75,7 @@ def main():
         drafter = NgramDrafter(block=a.spec_block)
     eng = Engine(model, num_pages=a.requests * pages_per_req + 64, page_size=a.page_size,
                  max_running=a.requests, max_prefill_tokens=a.max_prefill_tokens, tp=tp,
-                 tp_shards=shards, drafter=drafter)
+                 tp_shards=shards, drafter=drafter, cuda_graphs=a.cuda_graphs and world == 1)
     if rank != 0:
         eng.runner.follow()
         tp.shutdown()
@@ -143,6 +144,9 @@ def main():
         out["decode_step_ms"] = round(dec / max(1, a.gen - 1) * 1000, 2)
     if tp is not None:
         out["fused_allreduce_calls"] = tp.fused_calls
+    if eng.runner.graphs is not None:
+        out["cuda_graphs"] = {"captured": len(eng.runner.graphs.graphs),
+                              "replays": eng.runner.graphs.replays}
     if drafter is not None:
         out["spec"] = {"drafter": a.spec, "block": a.spec_block,
                        "accept_length": round(eng.spec_accept_length, 3),

@@ -31,7 +31,7 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
                     c10::optional<torch::Tensor> bias, torch::Tensor offsets, torch::Tensor counts,
                     int64_t epi, c10::optional<torch::Tensor> row_scale, torch::Tensor out,
                     double act_alpha, double act_limit, int64_t bn,
-                    c10::optional<torch::Tensor> lora_b, c10::optional<torch::Tensor> xa);
+                    c10::optional<torch::Tensor> lora_b, c10::optional<torch::Tensor> xa, int64_t int_cvt);
 void moe_route(torch::Tensor logits, torch::Tensor ids, torch::Tensor gates, bool replay);
 void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor offsets,
                torch::Tensor expert_counts, torch::Tensor dest, torch::Tensor row_src,
@@ -98,7 +98,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("x"), py::arg("blocks"), py::arg("scales"), py::arg("bias"), py::arg("offsets"),
         py::arg("counts"), py::arg("epi"), py::arg("row_scale"), py::arg("out"),
         py::arg("act_alpha") = 1.702, py::arg("act_limit") = 7.0, py::arg("bn") = 32,
-        py::arg("lora_b") = py::none(), py::arg("xa") = py::none());
+        py::arg("lora_b") = py::none(), py::arg("xa") = py::none(), py::arg("int_cvt") = 0);
   m.def("moe_route", &af3::moe_route);
   m.def("moe_group", &af3::moe_group);
   m.def("gather_rows", &af3::gather_rows);

@@ -76,6 +76,7 @@ struct Params {
   int64_t ldo;
   float act_alpha, act_limit;
   int* err;
+  int int_cvt;                // 1: integer e2m1 -> f16 conversion (scales <= 128), 0: cvt
 };
 
 template <int BN>
@@ -309,12 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();                        // the warp's packed bytes are in registers
           if (lane == 0) mbar_arrive(&pack_empty[ps]);
           ++ip;
-          const uint32_t s0 = e8m0_to_f16_bits(row_ok ? my_scales[2 * kb] : 127u);
-          const uint32_t s1 = e8m0_to_f16_bits(row_ok ? my_scales[2 * kb + 1] : 127u);
-          e2m1x32_to_f16x32(w0, s0, v);
-          tmem_st_32x32b_x16(ta, v);
-          e2m1x32_to_f16x32(w1, s1, v);
-          tmem_st_32x32b_x16(ta + 16, v);
+          const uint32_t r0 = row_ok ? my_scales[2 * kb] : 127u;
+          const uint32_t r1 = row_ok ? my_scales[2 * kb + 1] : 127u;
+          if (p.int_cvt) {
+            e2m1x32_to_f16x32_int(w0, e8m0_to_f16x2_int_scale(r0), v);
+            tmem_st_32x32b_x16(ta, v);
+            e2m1x32_to_f16x32_int(w1, e8m0_to_f16x2_int_scale(r1), v);
+            tmem_st_32x32b_x16(ta + 16, v);
+          } else {
+            e2m1x32_to_f16x32(w0, e8m0_to_f16_bits(r0), v);
+            tmem_st_32x32b_x16(ta, v);
+            e2m1x32_to_f16x32(w1, e8m0_to_f16_bits(r1), v);
+            tmem_st_32x32b_x16(ta + 16, v);
+          }
         } else {
           // LoRA block: row f of B_e (bf16, K2 wide) -> f16; zeros past K2 and past N
           const int k2 = (kb - kb_w) * kBK;
@@ -452,11 +460,14 @@ void launch(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tx2
 //   epi 1   row_scale[r] * (...) -> out bf16 [R, N]
 //   bn      token tile (16, 32, 64 or 128): ~ the largest number of rows per expert
 //   lora_b  optional bf16 [E, N, r] and xa bf16 [R, r] (= x A_e^T * scale): adds xa B_e^T
+//   int_cvt 1: integer e2m1 -> f16 conversion, valid when every scale byte is <= 128 (the
+//           caller checks); 0: the hardware cvt path (scales <= 140)
 void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
                     c10::optional<torch::Tensor> bias, torch::Tensor offsets, torch::Tensor counts,
                     int64_t epi, c10::optional<torch::Tensor> row_scale, torch::Tensor out,
                     double act_alpha, double act_limit, int64_t bn,
-                    c10::optional<torch::Tensor> lora_b, c10::optional<torch::Tensor> xa) {
+                    c10::optional<torch::Tensor> lora_b, c10::optional<torch::Tensor> xa,
+                    int64_t int_cvt) {
   using namespace mxm;
   check_cuda_bf16(x, "x");
   check_cuda_bf16(out, "out");
@@ -535,6 +546,7 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
   p.act_alpha = (float)act_alpha;
   p.act_limit = (float)act_limit;
   p.err = device_error_ptr();
+  p.int_cvt = int_cvt ? 1 : 0;
 #define AF3_MXM(B)                                                                  \
   case B:                                                                           \
     if (epi == kSwiglu) launch<B, kSwiglu>(tw, tx, tx2, p, stream);                 \

@@ -75,6 +75,35 @@ __device__ __forceinline__ void e2m1x32_to_f16x32(uint4 w, uint32_t scale_f16_bi
   }
 }
 
+// 16 packed bytes (32 e2m1 values) -> 16 f16x2 words with integer operations only.  The three
+// magnitude bits (e1 e0 m) of a nibble placed at f16 bits 11..9, with its sign at bit 15, encode
+// exactly value * 2^-14 (exponent field e1e0 with bias 15; e = 0 gives the subnormal
+// (m / 2) * 2^-14).  Per byte: one byte permute, two integer multiplies that place the low
+// nibble at bits 9 / 15 and the high nibble at bits 25 / 31 (b * 0x1001 repeats the byte 12
+// bits up), one lop3, then one f16x2 multiply by `scale2` = 2^(s-113) in both halves, which
+// gives value * 2^(s-127) exactly whenever that is an f16 number.  Requires s in [99, 128].
+__device__ __forceinline__ void e2m1x32_to_f16x32_int(uint4 w, uint32_t scale2, uint32_t (&v)[16]) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t b = __byte_perm(in[i], 0u, 0x4440u + j);   // byte j, zero-extended
+      const uint32_t d9 = b * 0x00200200u;                      // (b * 0x1001) << 9
+      const uint32_t d12 = b * 0x01001000u;                     // (b * 0x1001) << 12
+      uint32_t o = (d9 & 0x0E000E00u) | (d12 & 0x80008000u);
+      asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o) : "r"(scale2));
+      v[4 * i + j] = o;
+    }
+  }
+}
+
+// f16x2 bits of 2^(s-113) in both halves (s in [99, 128]): the factor of the integer path.
+__device__ __forceinline__ uint32_t e8m0_to_f16x2_int_scale(uint32_t s) {
+  const uint32_t h = (s - 98u) << 10;
+  return h | (h << 16);
+}
+
 // f16 bits of 2^(s-127): normal for s >= 113, subnormal 2^-24 * 2^(s-103) for s in [103, 112].
 __device__ __forceinline__ uint32_t e8m0_to_f16_bits(uint32_t s) {
   return s >= 113 ? ((s - 112) << 10) : (1u << (s - 103));

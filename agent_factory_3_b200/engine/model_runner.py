@@ -53,6 +53,7 @@ class ModelRunner:
         self.lora_active = lora_active
         self.device = model.embed_tokens.device
         self._bd_cache: dict = {}
+        self.graphs = None      # engine.cuda_graph.DecodeGraphs when decode steps are captured
 
     def _qkv_lora(self, attn):
         if not self.lora_active:
@@ -176,12 +177,11 @@ class ModelRunner:
         logits = matmul(hl, self.model.lm_head, out_dtype=torch.float32)
         return StepOutput(logits=logits, routing=routing, item_rows=m.rows, logit_offsets=offs)
 
-    @torch.inference_mode()
-    def forward(self, items: list[StepItem]) -> StepOutput:
+    def _layers(self, m: "_Meta", x: torch.Tensor) -> tuple[torch.Tensor, list]:
+        """All decoder layers over the packed new tokens; returns the final hidden states and
+        the per-layer routed expert ids."""
         cfg = self.cfg
-        m = self._meta(items)
         rope = self.model.rope(self.device)
-        x = torch.nn.functional.embedding(m.ids_t, self.model.embed_tokens)
         rec: list = []
         for li, layer in enumerate(self.model.layers):
             a, mlp = layer.self_attn, layer.mlp
@@ -203,6 +203,17 @@ class ModelRunner:
                                 cfg.num_experts_per_tok, None, 1.0, None, cfg.swiglu_alpha,
                                 cfg.swiglu_limit, lay_rec)
             rec.append(lay_rec[0])
+        return x, rec
+
+    @torch.inference_mode()
+    def forward(self, items: list[StepItem]) -> StepOutput:
+        if self.graphs is not None:
+            out = self.graphs.run(items)
+            if out is not None:
+                return out
+        m = self._meta(items)
+        x = torch.nn.functional.embedding(m.ids_t, self.model.embed_tokens)
+        x, rec = self._layers(m, x)
         return self._finish(m, items, x, rec)
 
 

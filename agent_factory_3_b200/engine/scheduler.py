@@ -15,6 +15,7 @@ from __future__ import annotations
 import base64
 import itertools
 import logging
+import os
 import queue
 import threading
 import time
@@ -79,7 +80,7 @@ class Engine:
     def __init__(self, model, *, num_pages: int = 4096, page_size: int = 64,
                  max_running: int = 128, max_prefill_tokens: int = 16384,
                  max_context_tokens: Optional[int] = None, weight_version: str = "0",
-                 tp=None, tp_shards=None, drafter=None):
+                 tp=None, tp_shards=None, drafter=None, cuda_graphs: Optional[bool] = None):
         """``tp``: an ``engine.tp.TPContext`` to run tensor-parallel (this process is one rank;
         rank 0 runs the scheduler, the others call ``self.runner.follow()``)."""
         self.model = model
@@ -94,6 +95,11 @@ class Engine:
             self.runner = TPModelRunner(model, self.kv, tp, tp_shards)
         else:
             self.runner = ModelRunner(model, self.kv, lora_active=False)
+            if cuda_graphs is None:
+                cuda_graphs = os.environ.get("AF3_CUDA_GRAPHS") == "1"
+            if cuda_graphs and dev.type == "cuda":
+                from .cuda_graph import DecodeGraphs
+                self.runner.graphs = DecodeGraphs(self.runner)
         self.tp = tp
         self.drafter = drafter          # engine.spec drafter: speculative decoding when set
         self.spec_verifies = 0

@@ -229,6 +229,7 @@ def main():
                     help="block: one-forward block draft model sharing the target's embeddings")
     ap.add_argument("--speculative-num-draft-tokens", type=int, default=8)
     ap.add_argument("--speculative-draft-layers", type=int, default=1)
+    ap.add_argument("--cuda-graphs", action="store_true", help="replay decode steps from CUDA graphs (TP=1)")
     a = ap.parse_args()
     from pathlib import Path
     p = Path(a.model)
@@ -268,7 +269,8 @@ def main():
         drafter = NgramDrafter(block=a.speculative_num_draft_tokens)
     eng = Engine(model, num_pages=a.num_pages, page_size=a.page_size,
                  max_running=a.max_running_requests, max_prefill_tokens=a.max_prefill_tokens,
-                 tp=tp, tp_shards=shards, drafter=drafter)
+                 tp=tp, tp_shards=shards, drafter=drafter,
+                 cuda_graphs=a.cuda_graphs and world == 1)
     if rank != 0:
         eng.runner.follow()
         tp.shutdown()

@@ -31,7 +31,7 @@ from ..ops import gemm as G
 from ..ops import moe as M
 from ..ops import mxfp4
 from ..ops._ext import ext, use_cuda_kernels
-from ..ops.moe_layer import ExpertWeights, _token_tile
+from ..ops.moe_layer import ExpertWeights, _token_tile, mxfp4_int_cvt
 from ..ops.norm import rmsnorm, rmsnorm_reference
 from .model_runner import ModelRunner, StepItem, StepOutput
 
@@ -262,12 +262,14 @@ def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int,
         h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
         bn = _token_tile(T * top_k, n_experts)
         xa = G.grouped_matmul(x_s, lora.gu_A, rt.offsets, alpha=lora.s_mlp)[0] if gu_lora else None
+        ic = mxfp4_int_cvt(ex)
         ext().moe_mxfp4_gemm(x_s, ex.gu_blocks, ex.gu_scales, ex.gu_bias, offs, cnts, 0, None, h,
-                             alpha, limit, bn, lora_b=lora.gu_B if gu_lora else None, xa=xa)
+                             alpha, limit, bn, lora_b=lora.gu_B if gu_lora else None, xa=xa,
+                             int_cvt=ic)
         ha = G.grouped_matmul(h, lora.dn_A, rt.offsets, alpha=lora.s_mlp)[0] if dn_lora else None
         ext().moe_mxfp4_gemm(h, ex.dn_blocks, ex.dn_scales, ex.dn_bias, offs, cnts, 1,
                              rt.row_gate, y_s, alpha, limit, bn,
-                             lora_b=lora.dn_B if dn_lora else None, xa=ha)
+                             lora_b=lora.dn_B if dn_lora else None, xa=ha, int_cvt=ic)
     else:
         W_gu = mxfp4.dequantize(ex.gu_blocks, ex.gu_scales)
         W_dn = mxfp4.dequantize(ex.dn_blocks, ex.dn_scales)

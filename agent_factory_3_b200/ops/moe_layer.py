@@ -68,6 +68,19 @@ class ExpertWeights:
         cls._scratch.clear()
 
     _f16_ok: dict = {}
+    _int_ok: dict = {}
+
+    def int_cvt_ok(self) -> bool:
+        """True when every block scale s is <= 128 (cached per tensor version)."""
+        ok = True
+        for sc in (self.gu_scales, self.dn_scales):
+            key = (sc.data_ptr(), sc._version, sc.numel())
+            v = self._int_ok.get(key)
+            if v is None:
+                v = bool((sc <= 128).all())
+                self._int_ok[key] = v
+            ok = ok and v
+        return ok
 
     def f16_exact(self) -> bool:
         """True when every block scale s lies in [104, 140]: then each e2m1 value times
@@ -87,6 +100,14 @@ class ExpertWeights:
 
 def _b(t):
     return None if t is None else t.to(torch.bfloat16)
+
+
+def mxfp4_int_cvt(experts: ExpertWeights) -> int:
+    """1 when the MXFP4-direct kernel may use its integer e2m1 -> f16 conversion (every scale
+    byte <= 128); AF3_MXFP4_CVT=hw forces the hardware conversion instruction."""
+    if os.environ.get("AF3_MXFP4_CVT") == "hw":
+        return 0
+    return 1 if experts.int_cvt_ok() else 0
 
 
 class MoEFn(torch.autograd.Function):
@@ -196,14 +217,15 @@ def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, 
     gu_A, gu_B, dn_A, dn_B = (lora.get(k) for k in ("gu_A", "gu_B", "dn_A", "dn_B"))
     xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if gu_A is not None else None
     h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
+    ic = mxfp4_int_cvt(experts)
     ext().moe_mxfp4_gemm(x_s, experts.gu_blocks, experts.gu_scales, experts.gu_bias, rt.offsets,
                          rt.counts, 0, None, h, act_alpha, act_limit, bn,
-                         lora_b=_b(gu_B) if xa is not None else None, xa=xa)
+                         lora_b=_b(gu_B) if xa is not None else None, xa=xa, int_cvt=ic)
     ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if dn_A is not None else None
     y_s = torch.empty(R, H, device=xn.device, dtype=torch.bfloat16)
     ext().moe_mxfp4_gemm(h, experts.dn_blocks, experts.dn_scales, experts.dn_bias, rt.offsets,
                          rt.counts, 1, rt.row_gate, y_s, act_alpha, act_limit, bn,
-                         lora_b=_b(dn_B) if ha is not None else None, xa=ha)
+                         lora_b=_b(dn_B) if ha is not None else None, xa=ha, int_cvt=ic)
     return M.combine_rows(y_s, rt.dest, top_k, residual=residual)
 
 

@@ -51,15 +51,17 @@ def _case(dev, E=6, N=256, K=192, r=0, seed=0):
 
 @pytest.mark.parametrize("bn", [16, 32, 64, 128])
 @pytest.mark.parametrize("r", [0, 32])
-def test_moe_mxfp4_gemm_matches_reference(dev, bn, r):
+@pytest.mark.parametrize("int_cvt", [0, 1])
+def test_moe_mxfp4_gemm_matches_reference(dev, bn, r, int_cvt):
     d, pre, valid, row_scale = _case(dev, r=r, seed=bn + r)
     R, N = pre.shape
     out_sw = torch.full((R, N // 2), 7.0, device=dev, dtype=torch.bfloat16)
     ext().moe_mxfp4_gemm(d["x"], d["blocks"], d["scales"], d["bias"], d["offsets"], d["counts"], 0,
-                         None, out_sw, 1.702, 7.0, bn, lora_b=d["lb"], xa=d["xa"])
+                         None, out_sw, 1.702, 7.0, bn, lora_b=d["lb"], xa=d["xa"], int_cvt=int_cvt)
     out_rs = torch.full((R, N), 7.0, device=dev, dtype=torch.bfloat16)
     ext().moe_mxfp4_gemm(d["x"], d["blocks"], d["scales"], d["bias"], d["offsets"], d["counts"], 1,
-                         d["row_scale"], out_rs, 1.702, 7.0, bn, lora_b=d["lb"], xa=d["xa"])
+                         d["row_scale"], out_rs, 1.702, 7.0, bn, lora_b=d["lb"], xa=d["xa"],
+                         int_cvt=int_cvt)
     torch.cuda.synchronize()
     assert ext().device_error() == 0
     q = pre.bfloat16().float()                      # the epilogue rounds gate/up to bf16 first
@@ -108,3 +110,25 @@ def test_scale_range_guard(dev):
         assert not _mxfp4_direct(x, ExpertWeights(b, bad, None, b, good, None), E, 2)
         good[1, 1, 1] = 150          # in-place change: re-checked through the tensor version
         assert not _mxfp4_direct(x, ex, E, 2)
+
+
+def test_integer_and_hardware_conversion_agree_bitwise(dev):
+    """Both e2m1 -> f16 conversions are exact, so over every byte pattern and every scale the
+    integer path allows (104..128) the two kernels must produce identical outputs."""
+    g = torch.Generator().manual_seed(9)
+    E, N, K, R = 2, 256, 512, 64
+    blocks = torch.randint(0, 256, (E, N, K // 32, 16), generator=g, dtype=torch.uint8)
+    scales = torch.randint(104, 129, (E, N, K // 32), generator=g, dtype=torch.uint8)
+    x = (torch.randn(R, K, generator=g) * 0.5).bfloat16()
+    offsets = torch.tensor([0, 32, 64], dtype=torch.int32)
+    counts = torch.tensor([32, 32], dtype=torch.int32)
+    row_scale = torch.rand(R, generator=g)
+    outs = []
+    for ic in (0, 1):
+        o = torch.zeros(R, N, device=dev, dtype=torch.bfloat16)
+        ext().moe_mxfp4_gemm(x.to(dev), blocks.to(dev), scales.to(dev), None, offsets.to(dev),
+                             counts.to(dev), 1, row_scale.to(dev), o, 1.702, 7.0, 32, int_cvt=ic)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert ext().device_error() == 0
+    assert torch.equal(outs[0], outs[1])
