@@ -36,6 +36,9 @@ def main():
                     help="speculative decoding: block = 1-layer random-init block draft model")
     ap.add_argument("--spec-block", type=int, default=8)
     ap.add_argument("--cuda-graphs", action="store_true", help="replay decode steps from CUDA graphs (TP=1)")
+    ap.add_argument("--trace", default=None,
+                    help="write a per-kernel device-time table of the run to this path (profiled "
+                         "run: its throughput is not a benchmark number)")
     a = ap.parse_args()
 
     from ..engine.scheduler import Engine, Request
@@ -119,10 +122,20 @@ def main():
                     stream=True)   # per-step callbacks: the first token of each request is seen
         r.on_output = make_cb(r)
         reqs.append(r)
+    prof = None
+    if a.trace:
+        from torch.profiler import ProfilerActivity, profile
+        prof = profile(activities=[ProfilerActivity.CUDA])
+        prof.__enter__()
     t_start = time.perf_counter()
     for r in reqs:
         eng.submit(r)
     ok = all_done.wait(3600)
+    if prof is not None:
+        torch.cuda.synchronize()
+        prof.__exit__(None, None, None)
+        with open(a.trace, "w") as f:
+            f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40))
     steps = eng.step_count - steps0
     eng.stop()
     gen = sum(len(r.output_ids) for r in reqs)

@@ -25,8 +25,8 @@
 // weights and was bound by shared-memory bandwidth.
 //
 // Warp roles (768 threads, persistent CTAs over tiles (expert, 128-feature tile, token tile)):
-//   warp 0      TMA: packed weight rows [128 x 32 bytes] per 64-wide K block into a 24-stage
-//               ring (96 KB in flight per SM: the latency x bandwidth product of HBM)
+//   warp 0      TMA: packed weight rows [128 x 32 bytes] per 64-wide K block into a 32-stage
+//               ring (128 KB in flight per SM: above the latency x bandwidth product of HBM)
 //   warp 3      TMA: the f16 token tile [BN x 64] per K block into its own ring; each tile's
 //               e8m0 scales (one contiguous block) by a bulk copy into a double buffer.  With
 //               LoRA, ceil(r/64) more K blocks follow: the rows' x A_e^T * scale as the token
@@ -55,7 +55,7 @@ constexpr int kMaxScaleCols = 96;   // K / 32 <= 96 (K <= 3072)
 constexpr int kBM = 128;    // weight rows per tile
 constexpr int kBK = 64;     // K per pipeline stage (one 128-byte f16 swizzle row)
 constexpr int kAStages = 8;       // converted-weight stages in TMEM (32 columns each)
-constexpr int kPackStages = 24;   // packed-weight stages (TMA: latency x bandwidth)
+constexpr int kPackStages = 32;   // packed-weight stages (TMA: latency x bandwidth)
 constexpr int kMaxExperts = 512;
 constexpr int kTmemCols = 512;    // [0, 2 BN) accumulators, [256, 512) A stages
 constexpr int kACol = 256;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;               // weight row of the tile = TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int kblk = p.K / 32;
-    int it = 0, ip = 0, tc = 0;
+    int it_base = 0, ip_base = 0, tc = 0;   // blocks / packed blocks of the earlier tiles
     bool ok = true;
     Tile tl;
     for (int t = blockIdx.x; ok && tile_of<BN>(t, p, prefix, tl); t += gridDim.x, ++tc) {
@@ -289,12 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* my_scales = tile_scales + b * C::SCALES + r * kblk;
       const int f = tl.f0 + r;
       const bool row_ok = f < p.N;
-      for (int kb = 0; kb < kb_n; ++kb, ++it) {
+      // this group's blocks of the tile: global block index it = g (mod kGroups)
+      for (int kb = (g - it_base) & (kGroups - 1); kb < kb_n; kb += kGroups) {
+        const int it = it_base + kb;
+        const int ip = ip_base + kb;            // packed-ring index (MXFP4 blocks only)
         const bool mx = kb < kb_w;
-        if ((it & (kGroups - 1)) != g) {
-          ip += mx ? 1 : 0;
-          continue;
-        }
         const int sa = it % kAStages;
         // the TMEM stage is free once the MMA of the block kAStages earlier has finished
         if (!mbar_wait(&a_empty[sa], ((it / kAStages) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
@@ -309,7 +308,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 w0 = src[0], w1 = src[1];
           __syncwarp();                        // the warp's packed bytes are in registers
           if (lane == 0) mbar_arrive(&pack_empty[ps]);
-          ++ip;
           const uint32_t r0 = row_ok ? my_scales[2 * kb] : 127u;
           const uint32_t r1 = row_ok ? my_scales[2 * kb + 1] : 127u;
           if (p.int_cvt) {
@@ -347,6 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[sa]);
       }
+      it_base += kb_n;
+      ip_base += kb_w;
       __syncwarp();                            // this warp is done with the tile's scales
       if (ok && lane == 0) mbar_arrive(&sc_empty[b]);
     }
