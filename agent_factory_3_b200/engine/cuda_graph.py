@@ -58,6 +58,7 @@ class _Graph:
         m.dec_pt, m.dec_lens = self.pt, self.lens
         m.dec_rows = torch.arange(B, device=dev, dtype=torch.long)
         m.dec_max = chunks * 16 * P
+        m.dec_identity = True
         self.m = m
         self.runner = runner
 

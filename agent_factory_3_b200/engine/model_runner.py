@@ -102,6 +102,7 @@ class ModelRunner:
             m.dec_lens = torch.tensor(lens, device=dev, dtype=torch.int32)
             m.dec_rows = torch.tensor(drows, device=dev, dtype=torch.long)
             m.dec_max = int(max(lens))
+            m.dec_identity = (not pre_idx) and drows == list(range(len(ids)))
         if pre_idx:   # packed full contexts of the prefill chunks
             ctx_slots, new_in_ctx, new_rows, tiles, cu = [], [], [], [], [0]
             for i in pre_idx:
@@ -137,6 +138,10 @@ class ModelRunner:
         apply_rope_(qkv, hq + hkv, d, m.pos_t, cos, sin)
         kp, vp = self.kv.k[li], self.kv.v[li]
         D.kv_store(qkv, qs, qs + kvs, m.slots_t, kp, vp)
+        if m.dec_idx and not m.pre_idx and getattr(m, "dec_identity", False):
+            # every row is a decode row, in order: no gather / scatter around the kernel
+            return D.decode_attention(qkv[:, :qs], kp, vp, m.dec_pt, m.dec_lens, sinks, hq, hkv,
+                                      window, scale, m.dec_max)
         o = torch.empty(m.N, qs, device=dev, dtype=qkv.dtype)
         if m.dec_idx:
             q = qkv.index_select(0, m.dec_rows)
