@@ -37,7 +37,7 @@ void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor 
                torch::Tensor expert_counts, torch::Tensor dest, torch::Tensor row_src,
                torch::Tensor row_gate, torch::Tensor scratch);
 void gather_rows(torch::Tensor x, torch::Tensor src, c10::optional<torch::Tensor> scale,
-                 torch::Tensor out);
+                 torch::Tensor out, bool zero_pad);
 void combine_rows(torch::Tensor y, torch::Tensor dest, int64_t K,
                   c10::optional<torch::Tensor> residual, torch::Tensor out);
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y,
@@ -101,7 +101,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lora_b") = py::none(), py::arg("xa") = py::none(), py::arg("int_cvt") = 0);
   m.def("moe_route", &af3::moe_route);
   m.def("moe_group", &af3::moe_group);
-  m.def("gather_rows", &af3::gather_rows);
+  m.def("gather_rows", &af3::gather_rows, py::arg("x"), py::arg("src"), py::arg("scale"),
+        py::arg("out"), py::arg("zero_pad") = true);
   m.def("combine_rows", &af3::combine_rows);
   m.def("rmsnorm_fwd", &af3::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &af3::rmsnorm_bwd);

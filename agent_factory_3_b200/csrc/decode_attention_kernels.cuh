@@ -129,14 +129,32 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attn_kernel(const Params p
       o1[h] *= a;
       m[h] = mn;
     }
-    // values: lane owns dims 2*lane, 2*lane+1
+    // values: lane owns dims 2*lane, 2*lane+1.  The lane's words of all 32 keys are loaded
+    // first (independent loads in flight together), then consumed from registers; the 32 keys
+    // span at most two pages when a page holds >= 32 tokens.
     const int nk = min(32, c_hi - base);
-    for (int j = 0; j < nk; ++j) {
-      const int kk = base + j;
-      const int page = pt[kk / p.page_size];
-      const __nv_bfloat162 vv = reinterpret_cast<const __nv_bfloat162*>(
-          p.vp + ((int64_t)page * p.page_size + kk % p.page_size) * tok_stride + g * kD)[lane];
-      const float2 vf = __bfloat1622float2(vv);
+    __nv_bfloat162 vreg[32];
+    {
+      const int pa = pt[base / p.page_size];
+      const int pb = pt[min(base + 31, c_hi - 1) / p.page_size];
+      const int first_page = base / p.page_size;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int kk = base + j;
+        if (j < nk) {
+          const int page = p.page_size >= 32 ? ((kk / p.page_size == first_page) ? pa : pb)
+                                              : pt[kk / p.page_size];
+          vreg[j] = reinterpret_cast<const __nv_bfloat162*>(
+              p.vp + ((int64_t)page * p.page_size + kk % p.page_size) * tok_stride + g * kD)[lane];
+        } else {
+          vreg[j] = __floats2bfloat162_rn(0.f, 0.f);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j >= nk) break;
+      const float2 vf = __bfloat1622float2(vreg[j]);
 #pragma unroll
       for (int h = 0; h < G; ++h) {
         const float ph = __shfl_sync(0xffffffff, pr[h], j);

@@ -408,29 +408,36 @@ namespace af3 {
 namespace mxm {
 
 // Token rows bf16 -> contiguous f16 for the kernel's TMA (the tensor core reads both operands
-// of kind::f16 as f16).  Rows [R, C] with unit inner stride, C % 8 == 0.
+// of kind::f16 as f16).  Only the rows the experts own are converted: rows
+// [offsets[e], offsets[e] + counts[e]) for each expert e (block y = expert); the padding rows of
+// the segments stay uninitialised -- they only ever feed token columns the epilogue drops.
 __global__ void rows_bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                                        uint4* __restrict__ y, int64_t R, int c8) {
-  const int64_t n = R * c8;
+                                        uint4* __restrict__ y, int c8,
+                                        const int* __restrict__ offsets,
+                                        const int* __restrict__ counts) {
+  const int e = blockIdx.y;
+  const int64_t r0 = offsets[e];
+  const int64_t n = (int64_t)counts[e] * c8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / c8, c = i - row * c8;
-    y[i] = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(x + row * ldx) + c));
+    const int64_t row = r0 + i / c8, c = i % c8;
+    y[row * c8 + c] = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(x + row * ldx) + c));
   }
 }
 
-torch::Tensor rows_to_f16(const torch::Tensor& x, cudaStream_t stream) {
+torch::Tensor rows_to_f16(const torch::Tensor& x, const torch::Tensor& offsets,
+                          const torch::Tensor& counts, cudaStream_t stream) {
   AF3_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) % 8 == 0 && (x.stride(0) * 2) % 16 == 0 &&
                 reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
             "token rows must be [R, C] with C % 8 == 0 and 16-byte aligned rows");
   auto y = torch::empty({x.size(0), x.size(1)}, x.options().dtype(torch::kHalf));
-  const int64_t n = x.size(0) * (x.size(1) / 8);
-  if (n == 0) return y;
-  const int threads = 256;
-  const int64_t grid = std::min<int64_t>((n + threads - 1) / threads, (int64_t)num_sms() * 8);
-  rows_bf16_to_f16_kernel<<<(unsigned)grid, threads, 0, stream>>>(
+  const int E = (int)counts.numel();
+  if (x.size(0) == 0 || E == 0) return y;
+  // rows per expert are few in decode: a handful of blocks per expert covers them
+  rows_bf16_to_f16_kernel<<<dim3(4, (unsigned)E), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
-      reinterpret_cast<uint4*>(y.data_ptr()), x.size(0), (int)(x.size(1) / 8));
+      reinterpret_cast<uint4*>(y.data_ptr()), (int)(x.size(1) / 8), offsets.data_ptr<int>(),
+      counts.data_ptr<int>());
   AF3_CUDA_CHECK(cudaGetLastError());
   return y;
 }
@@ -506,7 +513,7 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
   const CUtensorMap tw = make_tmap(blocks.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wd, ws, wb,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
   auto stream = at::cuda::getCurrentCUDAStream();
-  const torch::Tensor x16 = rows_to_f16(x, stream);
+  const torch::Tensor x16 = rows_to_f16(x, offsets, counts, stream);
   const uint64_t xd[2] = {(uint64_t)K, (uint64_t)x.size(0)};
   const uint64_t xs[1] = {(uint64_t)K * 2};
   const uint32_t xb[2] = {kBK, (uint32_t)bn};
@@ -524,7 +531,7 @@ void moe_mxfp4_gemm(torch::Tensor x, torch::Tensor blocks, torch::Tensor scales,
                   lora_b->is_contiguous() && (r * 2) % 16 == 0, "lora_b must be [E, N, r], r % 8 == 0");
     AF3_CHECK(xa->dim() == 2 && xa->size(0) == x.size(0) && xa->size(1) == r && xa->stride(1) == 1,
               "xa must be [R, r]");
-    xa16 = rows_to_f16(*xa, stream);
+    xa16 = rows_to_f16(*xa, offsets, counts, stream);
     const uint64_t ad[2] = {(uint64_t)r, (uint64_t)x.size(0)};
     const uint64_t as[1] = {(uint64_t)r * 2};
     tx2 = make_tmap(xa16.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ad, as, xb,

@@ -249,14 +249,15 @@ void moe_group(torch::Tensor ids, torch::Tensor gates, int64_t E, torch::Tensor 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                    const int* __restrict__ src, const float* __restrict__ scale,
                                    __nv_bfloat16* __restrict__ out, int64_t ldo, int64_t R,
-                                   int H) {
+                                   int H, int zero_pad) {
   const int vec = H / 8;
   for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
     const int s = src[r];
     const float sc = scale ? scale[r] : 1.f;
     uint4* o = reinterpret_cast<uint4*>(out + r * ldo);
     if (s < 0) {
-      for (int j = threadIdx.x; j < vec; j += blockDim.x) o[j] = make_uint4(0, 0, 0, 0);
+      if (zero_pad)
+        for (int j = threadIdx.x; j < vec; j += blockDim.x) o[j] = make_uint4(0, 0, 0, 0);
     } else {
       const uint4* xi = reinterpret_cast<const uint4*>(x + (int64_t)s * ldx);
       for (int j = threadIdx.x; j < vec; j += blockDim.x) {
@@ -276,7 +277,7 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
 }
 
 void gather_rows(torch::Tensor x, torch::Tensor src, c10::optional<torch::Tensor> scale,
-                 torch::Tensor out) {
+                 torch::Tensor out, bool zero_pad) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(out, "out");
   const int H = (int)x.size(1);
@@ -288,7 +289,7 @@ void gather_rows(torch::Tensor x, torch::Tensor src, c10::optional<torch::Tensor
   gather_rows_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), src.data_ptr<int>(),
       scale.has_value() ? scale->data_ptr<float>() : nullptr,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), R, H);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), R, H, zero_pad ? 1 : 0);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -249,13 +249,14 @@ def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int,
     rt = M.route(logits, top_k, n_experts)
     if routing_out is not None:
         routing_out.append(rt.ids)
-    x_s = M.gather_rows(xn, rt.row_src)
+    mx = xn.is_cuda and use_cuda_kernels(xn) and sh.experts.f16_exact()
+    x_s = M.gather_rows(xn, rt.row_src, zero_pad=not mx)   # the MXFP4 path never reads padding
     R = x_s.shape[0]
     ex = sh.experts
     y_s = torch.zeros(R, H, device=xn.device, dtype=torch.bfloat16)
     gu_lora = lora is not None and lora.gu_A is not None
     dn_lora = lora is not None and lora.dn_A is not None
-    if xn.is_cuda and use_cuda_kernels(xn) and ex.f16_exact():
+    if mx:
         offs = rt.offsets[sh.e0:sh.e1 + 1]
         cnts = rt.counts[sh.e0:sh.e1]
         I2 = ex.gu_blocks.shape[1]

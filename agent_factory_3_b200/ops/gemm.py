@@ -108,6 +108,11 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_layout: str = "mk", b_layout: 
             allowed = (256, 192, 128, 64)
         else:
             allowed = (256, 192, 128, 64, 32)
+        if M <= 128 and N <= 16384 and not dual and not a_mn and not b_mn:
+            # one row of tiles (decode-sized M): narrow tiles so the N tiles cover the SMs
+            # instead of leaving most of them idle while a few stream all of B
+            narrow = [b for b in (32, 64, 128) if b in allowed and math.ceil(N / b) >= 148]
+            allowed = (max(narrow),) if narrow else (min(allowed),)
         bn = pick_bn(N, allowed)
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
     assert residual is None or epi == EPI_BF16

@@ -102,8 +102,9 @@ def route(logits: torch.Tensor, top_k: int, n_experts: int,
 
 
 def gather_rows(x: torch.Tensor, row_src: torch.Tensor, scale: torch.Tensor | None = None,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-    """out[r] = scale[r] * x[row_src[r]] (zero rows where row_src < 0)."""
+                out: torch.Tensor | None = None, zero_pad: bool = True) -> torch.Tensor:
+    """out[r] = scale[r] * x[row_src[r]]; rows with row_src < 0 (segment padding) are zeroed, or
+    with ``zero_pad=False`` left as they are (inference paths that never read them)."""
     R = row_src.numel()
     if not use_cuda_kernels(x):
         idx = row_src.long().clamp_min(0)
@@ -117,7 +118,7 @@ def gather_rows(x: torch.Tensor, row_src: torch.Tensor, scale: torch.Tensor | No
         return y
     if out is None:
         out = torch.empty(R, x.shape[1], device=x.device, dtype=x.dtype)
-    ext().gather_rows(x, row_src, scale, out)
+    ext().gather_rows(x, row_src, scale, out, zero_pad)
     return out
 
 

@@ -211,7 +211,7 @@ def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, 
     rt = M.route(logits, top_k, E, replay_ids=replay_ids)
     if routing_out is not None:
         routing_out.append(rt.ids)
-    x_s = M.gather_rows(xn, rt.row_src)
+    x_s = M.gather_rows(xn, rt.row_src, zero_pad=False)   # padding rows are never read
     R = x_s.shape[0]
     bn = _token_tile(T * top_k, E)
     I2 = experts.gu_blocks.shape[1]
