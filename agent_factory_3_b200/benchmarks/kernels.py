@@ -6,6 +6,7 @@
     python -m agent_factory_3_b200.benchmarks.kernels --op moe --tokens 32768
     python -m agent_factory_3_b200.benchmarks.kernels --op dequant --experts 128
     python -m agent_factory_3_b200.benchmarks.kernels --op moe_decode --tokens 128 --path mxfp4
+    python -m agent_factory_3_b200.benchmarks.kernels --op decode_attn --tokens 128 --seqlens 1024
 
 Each run prints one JSON line with the time per call, the achieved TFLOP/s (or GB/s) and the
 fraction of the measured peak in MEASURED_PEAKS.json (when present).
@@ -129,6 +130,26 @@ def bench_dequant(args):
     return {"bytes": blocks.numel() + scales.numel() + out.numel() * 2, "ms": ms}
 
 
+def bench_decode_attn(args):
+    """Paged decode attention: ``--tokens`` sequences of ``--seqlens`` cached tokens each (64-token
+    pages, scattered), one query token per sequence; bytes = K and V read once."""
+    from ..ops import decode as D
+    B, L, hq, hkv, d, P = args.tokens, int(args.seqlens.split(",")[0]), args.hq, args.hkv, 64, 64
+    npg = (L + P - 1) // P
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kp = torch.randn(B * npg + 1, P, hkv, d, device="cuda", generator=g).bfloat16()
+    vp = torch.randn_like(kp)
+    perm = torch.randperm(B * npg, device="cuda", generator=g).to(torch.int32)
+    pt = perm.view(B, npg)
+    lens = torch.full((B,), L, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, hq * d, device="cuda", generator=g).bfloat16()
+    sinks = torch.zeros(hq, device="cuda")
+    out = torch.empty_like(q)
+    ms = _time(lambda: D.decode_attention(q, kp, vp, pt, lens, sinks, hq, hkv, args.window, None, L,
+                                          out=out), args.iters, flush_bytes=256 << 20)
+    return {"bytes": 2 * B * L * hkv * d * 2, "ms": ms}
+
+
 def bench_moe_decode(args):
     """One gpt-oss-120b MoE layer (128 experts, top-4, H = I = 2880) at decode batch sizes:
     the MXFP4-direct path (AF3_MOE_MXFP4=1) or the dequantise + grouped GEMM path (=0).
@@ -178,7 +199,7 @@ def bench_peer_sync(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe", "dequant", "moe_decode",
-                                                  "peer_sync"])
+                                                  "peer_sync", "decode_attn"])
     ap.add_argument("--seqlens", default="8192")
     ap.add_argument("--hq", type=int, default=64)
     ap.add_argument("--hkv", type=int, default=8)
@@ -203,6 +224,8 @@ def main():
         r = bench_moe_decode(args)
     elif args.op == "peer_sync":
         r = bench_peer_sync(args)
+    elif args.op == "decode_attn":
+        r = bench_decode_attn(args)
     else:
         r = bench_moe(args)
     peak_tf, peak_bw, kind = _peaks()

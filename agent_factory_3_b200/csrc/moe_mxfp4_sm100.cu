@@ -24,7 +24,7 @@
 // tile in shared memory spent 16 KB of writes and 16 KB of MMA reads per 4 KB of packed
 // weights and was bound by shared-memory bandwidth.
 //
-// Warp roles (768 threads, persistent CTAs over tiles (expert, 128-feature tile, token tile)):
+// Warp roles (1024 threads, persistent CTAs over tiles (expert, 128-feature tile, token tile)):
 //   warp 0      TMA: packed weight rows [128 x 32 bytes] per 64-wide K block into a 32-stage
 //               ring (128 KB in flight per SM: above the latency x bandwidth product of HBM)
 //   warp 3      TMA: the f16 token tile [BN x 64] per K block into its own ring; each tile's
@@ -34,11 +34,12 @@
 //               the converters), so the low-rank term accumulates into the same TMEM tile
 //   warp 1      tcgen05.mma (kind::f16, A from TMEM, M=128, N=BN, K=16 x 4 per block) into a
 //               double-buffered TMEM accumulator
-//   warps 4-19  converters, four groups of four warps; group g converts the K blocks
-//               it = g (mod 4), so four blocks are in flight and the conversion latency of one
-//               overlaps the others.  Thread (warp % 4, lane) owns weight row 32 (warp % 4) +
-//               lane: 32 packed bytes -> 64 f16 -> 32 TMEM columns of an 8-stage ring
-//   warps 20-23 epilogue: thread t owns feature row t; bias, then clamped SwiGLU (gate / up are
+//   warps 4-27  converters, six groups of four warps; group g converts the K blocks
+//               it = g (mod 6), so six blocks are in flight and the conversion latency of one
+//               overlaps the others (the converters are issue-bound: more of them keep the
+//               schedulers busier).  Thread (warp % 4, lane) owns weight row 32 (warp % 4) +
+//               lane: 32 packed bytes -> 64 f16 -> 32 TMEM columns of a 6- or 12-stage ring
+//   warps 28-31 epilogue: thread t owns feature row t; bias, then clamped SwiGLU (gate / up are
 //               interleaved rows 2i / 2i+1, partner taken with a lane shuffle) or a per-row
 //               router-gate scale; bf16 stores of Y[token, feature]
 #include "common.h"
@@ -49,17 +50,15 @@
 namespace af3 {
 namespace mxm {
 
-constexpr int kThreads = 768;
-constexpr int kGroups = 4;          // converter groups of four warps (warps 4-19)
+constexpr int kThreads = 1024;
+constexpr int kGroups = 6;          // converter groups of four warps (warps 4-27)
+constexpr int kEpiWarp = 4 + 4 * kGroups;   // warps 28-31: epilogue
 constexpr int kMaxScaleCols = 96;   // K / 32 <= 96 (K <= 3072)
 constexpr int kBM = 128;    // weight rows per tile
 constexpr int kBK = 64;     // K per pipeline stage (one 128-byte f16 swizzle row)
-constexpr int kAStages = 8;       // converted-weight stages in TMEM (32 columns each)
 constexpr int kPackStages = 32;   // packed-weight stages (TMA: latency x bandwidth)
 constexpr int kMaxExperts = 512;
-constexpr int kTmemCols = 512;    // [0, 2 BN) accumulators, [256, 512) A stages
-constexpr int kACol = 256;
-static_assert(kPackStages % kGroups == 0 && kAStages % kGroups == 0, "ring / group mapping");
+constexpr int kTmemCols = 512;    // [0, 2 BN) accumulators, [kACol, 512) A stages
 
 enum Epi : int { kSwiglu = 0, kRowScale = 1 };
 
@@ -87,14 +86,21 @@ struct Cfg {
   static constexpr int X_RING = 0;
   static constexpr int PACK_RING = X_RING + X_STAGES * X;
   static constexpr int BARS = PACK_RING + kPackStages * PACK;
+  // converted-weight stages in TMEM (32 columns each): two per converter group when the
+  // accumulators leave room, else one
+  static constexpr int A_STAGES = BN <= 64 ? 2 * kGroups : kGroups;
+  static constexpr int ACOL = kTmemCols - A_STAGES * 32;
+  static constexpr int BAR_BYTES = 2048;
   // expert tile prefix, padded so the scale buffers after it stay 128-byte aligned (the bulk
   // copy that fills them needs a 16-byte aligned destination)
   static constexpr int PREFIX = ((kMaxExperts + 1) * 4 + 127) / 128 * 128;
   static constexpr int SCALES = kBM * kMaxScaleCols;   // one tile's e8m0 scales
-  static constexpr int SMEM = 1024 + BARS + 1024 + PREFIX + 2 * SCALES;   // double-buffered
-  static_assert((BARS + 1024 + PREFIX) % 16 == 0 && SCALES % 16 == 0, "bulk copy alignment");
+  static constexpr int SMEM = 1024 + BARS + BAR_BYTES + PREFIX + 2 * SCALES;   // double-buffered
+  static_assert((BARS + BAR_BYTES + PREFIX) % 16 == 0 && SCALES % 16 == 0, "bulk copy alignment");
+  static_assert((2 * A_STAGES + 2 * X_STAGES + 2 * kPackStages + 8) * 8 + 8 <= BAR_BYTES,
+                "barrier area");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(2 * BN <= kACol, "accumulators overlap the A stages");
+  static_assert(2 * BN <= ACOL, "accumulators overlap the A stages");
 };
 
 struct Tile {
@@ -140,9 +146,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BARS);
-  uint64_t* a_full = bars;                                   // [kAStages] converters done
-  uint64_t* a_empty = a_full + kAStages;                     // [kAStages] MMA done
-  uint64_t* x_full = a_empty + kAStages;                     // [X_STAGES] TMA landed
+  uint64_t* a_full = bars;                                   // [A_STAGES] converters done
+  uint64_t* a_empty = a_full + C::A_STAGES;                  // [A_STAGES] MMA done
+  uint64_t* x_full = a_empty + C::A_STAGES;                  // [X_STAGES] TMA landed
   uint64_t* x_empty = x_full + C::X_STAGES;                  // [X_STAGES] MMA done
   uint64_t* pack_full = x_empty + C::X_STAGES;               // [kPackStages] TMA landed
   uint64_t* pack_empty = pack_full + kPackStages;            // [kPackStages] converters read
@@ -152,8 +158,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* sc_empty = sc_full + 2;                          // [2] converters done with them
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* prefix = reinterpret_cast<int*>(smem + C::BARS + 1024);
-  uint8_t* tile_scales = smem + C::BARS + 1024 + C::PREFIX;   // [2][SCALES]
+  int* prefix = reinterpret_cast<int*>(smem + C::BARS + C::BAR_BYTES);
+  uint8_t* tile_scales = smem + C::BARS + C::BAR_BYTES + C::PREFIX;   // [2][SCALES]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int ft = (p.N + kBM - 1) / kBM;
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tma_w);
     tma_prefetch_desc(&tma_x);
     if (p.K2 > 0) tma_prefetch_desc(&tma_x2);
-    for (int s = 0; s < kAStages; ++s) {
+    for (int s = 0; s < C::A_STAGES; ++s) {
       mbar_init(&a_full[s], 4);   // the four warps of the converting group
       mbar_init(&a_empty[s], 1);
     }
@@ -256,11 +262,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + b * BN;
         for (int kb = 0; kb < kb_n; ++kb, ++it) {
-          const int sa = it % kAStages, sx = it % C::X_STAGES;
-          if (!mbar_wait(&a_full[sa], (it / kAStages) & 1, p.err, abort_flag) ||
+          const int sa = it % C::A_STAGES, sx = it % C::X_STAGES;
+          if (!mbar_wait(&a_full[sa], (it / C::A_STAGES) & 1, p.err, abort_flag) ||
               !mbar_wait(&x_full[sx], (it / C::X_STAGES) & 1, p.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = tmem + kACol + sa * 32;
+          const uint32_t a0 = tmem + C::ACOL + sa * 32;
           const uint32_t x0 = smem_u32(smem + C::X_RING + sx * C::X);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
@@ -273,9 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(&acc_full[b]);
       }
     }
-  } else if (warp >= 4 && warp < 20) {
+  } else if (warp >= 4 && warp < kEpiWarp) {
     // ------------------------- MXFP4 -> f16 converters --------------------------------
-    const int g = (warp - 4) >> 2;             // group: converts the K blocks it = g (mod 4)
+    const int g = (warp - 4) >> 2;             // group: converts the K blocks it = g (mod kGroups)
     const int q = warp & 3;                    // TMEM lane quadrant this warp may access
     const int r = q * 32 + lane;               // weight row of the tile = TMEM lane
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -290,15 +296,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int f = tl.f0 + r;
       const bool row_ok = f < p.N;
       // this group's blocks of the tile: global block index it = g (mod kGroups)
-      for (int kb = (g - it_base) & (kGroups - 1); kb < kb_n; kb += kGroups) {
+      for (int kb = ((g - it_base) % kGroups + kGroups) % kGroups; kb < kb_n; kb += kGroups) {
         const int it = it_base + kb;
         const int ip = ip_base + kb;            // packed-ring index (MXFP4 blocks only)
         const bool mx = kb < kb_w;
-        const int sa = it % kAStages;
-        // the TMEM stage is free once the MMA of the block kAStages earlier has finished
-        if (!mbar_wait(&a_empty[sa], ((it / kAStages) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
+        const int sa = it % C::A_STAGES;
+        // the TMEM stage is free once the MMA of the block A_STAGES earlier has finished
+        if (!mbar_wait(&a_empty[sa], ((it / C::A_STAGES) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ta = tmem + lane_base + kACol + sa * 32;
+        const uint32_t ta = tmem + lane_base + C::ACOL + sa * 32;
         uint32_t v[16];
         if (mx) {
           // 32 packed bytes (64 values) of row r: two scale blocks -> 32 TMEM columns
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();                            // this warp is done with the tile's scales
       if (ok && lane == 0) mbar_arrive(&sc_empty[b]);
     }
-  } else if (warp >= 20) {
+  } else if (warp >= kEpiWarp) {
     // ------------------------------------ epilogue -------------------------------------
     const int q = warp & 3;
     const int r = q * 32 + lane;
