@@ -45,6 +45,9 @@ def parse_args():
     ap.add_argument("--lora-alpha", type=int, default=64)
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--shard-optimizer", action="store_true",
+                    help="shard the LoRA optimizer state over the ranks (reduce-scatter + "
+                         "all-gather) instead of one all-reduce")
     ap.add_argument("--trace", default=None,
                     help="after the timed steps, run one more step under torch.profiler and write "
                          "its per-kernel device-time table (text) to this path")
@@ -208,7 +211,7 @@ def main():
         lora_target_modules=["q_proj", "k_proj", "v_proj", "o_proj", "gate_up_proj", "down_proj"],
         max_capacity=args.tokens, pad_to_multiple_of_training=1024, random_init_seed=0,
         use_routing_replay=True, gradient_checkpointing=True, lr_warmup_steps=0,
-        learning_rate=1e-5)
+        learning_rate=1e-5, shard_optimizer_state=args.shard_optimizer)
     t_init = time.perf_counter()
     trainer = ModelTrainer(tcfg, model_config=mcfg, device=device)
     torch.cuda.synchronize()
