@@ -87,7 +87,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
     case 1: decode_attn_kernel<1><<<grid, kWarps * 32, 0, stream>>>(p); break;
     case 2: decode_attn_kernel<2><<<grid, kWarps * 32, 0, stream>>>(p); break;
     case 4: decode_attn_kernel<4><<<grid, kWarps * 32, 0, stream>>>(p); break;
-    case 8: decode_attn_kernel<8><<<grid, kWarps * 32, 0, stream>>>(p); break;
+    case 8: decode_attn_mma_kernel<<<grid, kWarps * 32, 0, stream>>>(p); break;   // tensor cores
     case 16: decode_attn_kernel<16><<<grid, kWarps * 32, 0, stream>>>(p); break;
     default: AF3_CHECK(false, "GQA group must be 1, 2, 4, 8 or 16");
   }

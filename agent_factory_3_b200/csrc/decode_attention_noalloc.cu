@@ -193,7 +193,7 @@ __attribute__((visibility("default"))) int af3_decode_attention_noalloc(
     case 1: decode_attn_kernel<1><<<grid, kWarps * 32, 0, stream>>>(p); break;
     case 2: decode_attn_kernel<2><<<grid, kWarps * 32, 0, stream>>>(p); break;
     case 4: decode_attn_kernel<4><<<grid, kWarps * 32, 0, stream>>>(p); break;
-    case 8: decode_attn_kernel<8><<<grid, kWarps * 32, 0, stream>>>(p); break;
+    case 8: decode_attn_mma_kernel<<<grid, kWarps * 32, 0, stream>>>(p); break;   // tensor cores
     default: decode_attn_kernel<16><<<grid, kWarps * 32, 0, stream>>>(p); break;
   }
   cudaError_t e = cudaGetLastError();
