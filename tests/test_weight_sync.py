@@ -57,9 +57,9 @@ def _receiver(q_out, q_in, shapes):
     torch.cuda.set_device(1)
     st = StagingBuffer.for_tensors(shapes, "cuda:1")
     q_out.put(st.export())
-    q_in.get()                      # the writer is done
+    q_in.get(timeout=120)           # the writer is done (bounded: never outlive a failed test)
     q_out.put({k: v.float().cpu() for k, v in st.tensors().items()})
-    q_in.get()                      # keep the buffer alive until the parent has read
+    q_in.get(timeout=120)           # keep the buffer alive until the parent has read
 
 
 def _writer(exported, shapes, q_done):
@@ -78,17 +78,23 @@ def test_peer_write_across_processes_two_gpus():
     shapes = {"x": (128, 2880), "y": (5760, 32), "z": (8,)}
     ctx = mp.get_context("spawn")
     q_out, q_in, q_done = ctx.Queue(), ctx.Queue(), ctx.Queue()
-    rec = ctx.Process(target=_receiver, args=(q_out, q_in, shapes))
+    rec = ctx.Process(target=_receiver, args=(q_out, q_in, shapes), daemon=True)
     rec.start()
-    exported = q_out.get(timeout=120)
-    wr = ctx.Process(target=_writer, args=(exported, shapes, q_done))
-    wr.start()
-    want = q_done.get(timeout=120)
-    wr.join(60)
-    q_in.put(1)
-    got = q_out.get(timeout=120)
-    q_in.put(1)
-    rec.join(60)
+    wr = None
+    try:
+        exported = q_out.get(timeout=120)
+        wr = ctx.Process(target=_writer, args=(exported, shapes, q_done), daemon=True)
+        wr.start()
+        want = q_done.get(timeout=120)
+        wr.join(60)
+        q_in.put(1)
+        got = q_out.get(timeout=120)
+        q_in.put(1)
+        rec.join(60)
+    finally:
+        for p in (rec, wr):
+            if p is not None and p.is_alive():
+                p.kill()
     for k in shapes:
         assert torch.equal(got[k], want[k]), k
 
