@@ -42,13 +42,15 @@
 #include <mutex>
 
 #include "decode_attention_kernels.cuh"
+#include "decode_attention_noalloc.h"
 
 namespace {
 constexpr size_t kScratchBytes = size_t(16) << 20;
 constexpr size_t kScratchFloats = kScratchBytes / sizeof(float);
 }  // namespace
 
-// The scratch itself: one per device, part of this module's device image.
+// The scratch itself: one per device, part of this module's device image.  Host code must
+// not pass this name to a kernel: on the host it is a stand-in, not the device address.
 static __device__ __align__(256) float g_decode_scratch[kScratchFloats];
 
 namespace {
@@ -59,13 +61,6 @@ constexpr int kFloatsPerPartial = af3::dec::kD + 2;  // partial output + (max, s
 std::atomic<float*> g_scratch_ptr[kMaxDevices] = {};
 std::mutex g_setup_mutex;
 thread_local char g_last_error[256] = "";
-
-enum {
-  AF3_NOALLOC_OK = 0,
-  AF3_NOALLOC_INVALID_ARGUMENT = 1,
-  AF3_NOALLOC_TOO_LARGE = 2,
-  AF3_NOALLOC_CUDA_ERROR = 3,
-};
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -159,6 +154,27 @@ __attribute__((visibility("default"))) int af3_decode_attention_noalloc(
                 max_seq_len, (long long)max_pages * page_size);
   if (batch > 0 && (!q || !k_pages || !v_pages || !page_table || !seq_lens || !sinks || !out))
     return fail(AF3_NOALLOC_INVALID_ARGUMENT, "null device pointer");
+  // The kernels read q and the K/V page rows with 16-byte vector loads and write out per
+  // bf16 element; a misaligned operand would fault on the device, so refuse it here.
+  const long long row_elems = (long long)num_q_heads * kD;
+  auto misaligned = [](const void* ptr, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) != 0;
+  };
+  if (batch > 0) {
+    if (misaligned(q, 16) || misaligned(k_pages, 16) || misaligned(v_pages, 16))
+      return fail(AF3_NOALLOC_INVALID_ARGUMENT, "q, k_pages and v_pages must be 16-byte aligned");
+    if (ld_q % 8 != 0 || ld_q < row_elems)
+      return fail(AF3_NOALLOC_INVALID_ARGUMENT,
+                  "ld_q %lld must be a multiple of 8 and at least num_q_heads * 64 = %lld", ld_q,
+                  row_elems);
+    if (ld_out < row_elems)
+      return fail(AF3_NOALLOC_INVALID_ARGUMENT, "ld_out %lld is below num_q_heads * 64 = %lld",
+                  ld_out, row_elems);
+    if (misaligned(out, 2) || misaligned(page_table, 4) || misaligned(seq_lens, 4) ||
+        misaligned(sinks, 4) || (lse && misaligned(lse, 4)))
+      return fail(AF3_NOALLOC_INVALID_ARGUMENT,
+                  "out must be 2-byte aligned; page_table, seq_lens, sinks and lse 4-byte aligned");
+  }
   const long long chunk_tokens = (long long)kChunkPages * page_size;
   const long long chunks = max_seq_len > 0 ? (max_seq_len + chunk_tokens - 1) / chunk_tokens : 1;
   const long long need = (long long)batch * num_q_heads * chunks * kFloatsPerPartial;

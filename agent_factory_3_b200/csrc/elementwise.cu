@@ -272,34 +272,93 @@ void lse_merge(torch::Tensor parts, torch::Tensor label_logit, torch::Tensor log
 }
 
 // ----------------------------- standalone clamped SwiGLU --------------------------------
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
-// gate_up [M, 2I] interleaved -> out [M, I]
+// gate_up [M, 2I] interleaved -> out [M, I].  Each thread handles 8 (gate, up) pairs: two
+// 16-byte loads and one 16-byte store (scalar tail for counts not divisible by 8).
+__device__ __forceinline__ float swiglu_one(float g, float u, float alpha, float limit) {
+  const float gc = fminf(g, limit);
+  const float uc = fminf(fmaxf(u, -limit), limit);
+  return gc * sigmoidf_(alpha * gc) * (uc + 1.f);
+}
+
+__device__ __forceinline__ void swiglu_grad_one(float g, float u, float d, float alpha,
+                                                float limit, float& dg, float& du) {
+  const float gc = fminf(g, limit);
+  const float uc = fminf(fmaxf(u, -limit), limit);
+  const float s = sigmoidf_(alpha * gc);
+  du = (u >= -limit && u <= limit) ? d * gc * s : 0.f;
+  dg = (g <= limit) ? d * (uc + 1.f) * (s + gc * alpha * s * (1.f - s)) : 0.f;
+}
+
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out,
-                                  int64_t n_pairs, float alpha, float limit) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs;
-       i += (int64_t)gridDim.x * blockDim.x) {
+                                  int64_t n_pairs, int64_t n8, float alpha, float limit) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(gu) + 2 * i);
+    const uint4 b = __ldcs(reinterpret_cast<const uint4*>(gu) + 2 * i + 1);
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+    float h[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = __bfloat1622float2(pa[e]);
+      const float2 y = __bfloat1622float2(pb[e]);
+      h[e] = swiglu_one(x.x, x.y, alpha, limit);
+      h[4 + e] = swiglu_one(y.x, y.y, alpha, limit);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(h[0], h[1]);
+    o.y = pack_bf16x2(h[2], h[3]);
+    o.z = pack_bf16x2(h[4], h[5]);
+    o.w = pack_bf16x2(h[6], h[7]);
+    __stcs(reinterpret_cast<uint4*>(out) + i, o);
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs; i += stride) {
     const float2 gv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(gu)[i]);
-    const float gc = fminf(gv.x, limit);
-    const float uc = fminf(fmaxf(gv.y, -limit), limit);
-    out[i] = __float2bfloat16(gc * sigmoidf_(alpha * gc) * (uc + 1.f));
+    out[i] = __float2bfloat16(swiglu_one(gv.x, gv.y, alpha, limit));
   }
 }
 
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
                                   const __nv_bfloat16* __restrict__ dout,
-                                  __nv_bfloat16* __restrict__ dgu, int64_t n_pairs, float alpha,
-                                  float limit) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs;
-       i += (int64_t)gridDim.x * blockDim.x) {
+                                  __nv_bfloat16* __restrict__ dgu, int64_t n_pairs, int64_t n8,
+                                  float alpha, float limit) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(gu) + 2 * i);
+    const uint4 b = __ldcs(reinterpret_cast<const uint4*>(gu) + 2 * i + 1);
+    const uint4 dv = __ldcs(reinterpret_cast<const uint4*>(dout) + i);
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+    const __nv_bfloat162* pd = reinterpret_cast<const __nv_bfloat162*>(&dv);
+    uint32_t r[8];
+    // pairs 0..3 come from `a`, 4..7 from `b`; their output gradients are dout[8i .. 8i+7]
+    float dd[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 d = __bfloat1622float2(pd[e]);
+      dd[2 * e] = d.x;
+      dd[2 * e + 1] = d.y;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = __bfloat1622float2(pa[e]);
+      const float2 y = __bfloat1622float2(pb[e]);
+      float dg, du;
+      swiglu_grad_one(x.x, x.y, dd[e], alpha, limit, dg, du);
+      r[e] = pack_bf16x2(dg, du);
+      swiglu_grad_one(y.x, y.y, dd[4 + e], alpha, limit, dg, du);
+      r[4 + e] = pack_bf16x2(dg, du);
+    }
+    __stcs(reinterpret_cast<uint4*>(dgu) + 2 * i, make_uint4(r[0], r[1], r[2], r[3]));
+    __stcs(reinterpret_cast<uint4*>(dgu) + 2 * i + 1, make_uint4(r[4], r[5], r[6], r[7]));
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs; i += stride) {
     const float2 gv = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(gu)[i]);
-    const float d = __bfloat162float(dout[i]);
-    const float gc = fminf(gv.x, limit);
-    const float uc = fminf(fmaxf(gv.y, -limit), limit);
-    const float s = sigmoidf_(alpha * gc);
-    const float glu = gc * s;
-    const float du = (gv.y >= -limit && gv.y <= limit) ? d * glu : 0.f;
-    const float dg = (gv.x <= limit) ? d * (uc + 1.f) * (s + gc * alpha * s * (1.f - s)) : 0.f;
+    float dg, du;
+    swiglu_grad_one(gv.x, gv.y, __bfloat162float(dout[i]), alpha, limit, dg, du);
     reinterpret_cast<__nv_bfloat162*>(dgu)[i] = __floats2bfloat162_rn(dg, du);
   }
 }
@@ -310,10 +369,14 @@ void swiglu_fwd(torch::Tensor gu, torch::Tensor out, double alpha, double limit)
   const int64_t n = out.numel();
   const c10::cuda::CUDAGuard guard(gu.device());
   if (n == 0) return;
-  swiglu_fwd_kernel<<<std::min<int64_t>((n + 255) / 256, num_sms() * 16), 256, 0,
+  // 8 pairs per thread through 16-byte accesses when every operand is 16-byte aligned
+  const bool vec = aligned16(gu.data_ptr()) && aligned16(out.data_ptr());
+  const int64_t n8 = vec ? n / 8 : 0;
+  swiglu_fwd_kernel<<<std::min<int64_t>((std::max<int64_t>(n8, n - n8 * 8) + 255) / 256,
+                                        num_sms() * 8), 256, 0,
                       at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n, (float)alpha, (float)limit);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n, n8, (float)alpha, (float)limit);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -324,11 +387,14 @@ void swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu, double 
   const int64_t n = dout.numel();
   const c10::cuda::CUDAGuard guard(gu.device());
   if (n == 0) return;
-  swiglu_bwd_kernel<<<std::min<int64_t>((n + 255) / 256, num_sms() * 16), 256, 0,
+  const bool vec = aligned16(gu.data_ptr()) && aligned16(dout.data_ptr()) && aligned16(dgu.data_ptr());
+  const int64_t n8 = vec ? n / 8 : 0;
+  swiglu_bwd_kernel<<<std::min<int64_t>((std::max<int64_t>(n8, n - n8 * 8) + 255) / 256,
+                                        num_sms() * 8), 256, 0,
                       at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), n, (float)alpha, (float)limit);
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), n, n8, (float)alpha, (float)limit);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -199,6 +199,17 @@ class TPContext:
         xn = rmsnorm_reference(x, w, eps) if w is not None else None
         return x, xn
 
+    def raise_on_device_error(self) -> None:
+        """Read (and clear) the device error word after a step's fused reductions.  A peer
+        that did not arrive within ``timeout_s`` makes the reduction kernel give up without
+        writing its outputs; the step's hidden states are then garbage, so the step fails here
+        instead of decoding on.  The read synchronises the stream once per step."""
+        code = int(ext().device_error())
+        if code != 0:
+            raise RuntimeError(
+                f"tensor-parallel rank {self.rank}: fused all-reduce reported device error "
+                f"{code} (a peer rank did not arrive within {self.timeout_s} s); step aborted")
+
     # -- step broadcast (rank 0 -> others) -------------------------------------------------
     def send(self, msg) -> None:
         dist.broadcast_object_list([msg], group=self.cpu_group, group_src=0)
@@ -383,4 +394,7 @@ class TPModelRunner(ModelRunner):
             x, xn = self.ctx.allreduce_norm(part, h, nxt, eps)
         if self.ctx.rank != 0:   # only rank 0 samples
             items = [StepItem(it.ids, it.start, it.pages, False, False) for it in items]
-        return self._finish(m, items, x, rec)
+        out = self._finish(m, items, x, rec)
+        if self.ctx.symm is not None:
+            self.ctx.raise_on_device_error()
+        return out

@@ -50,9 +50,11 @@ class ExtraRoundConfig(BaseModel):
     @model_validator(mode="after")
     def _validate(self):
         if self.min_budget > self.budget:
-            raise ValueError(f"min_budget ({self.min_budget}) must be <= budget ({self.budget})")
-        if not self.on_token_limit and not self.on_max_rounds:
-            raise ValueError("At least one of on_token_limit/on_max_rounds must be True")
+            raise ValueError(f"extra round: the token floor min_budget={self.min_budget} is "
+                             f"above the budget {self.budget}")
+        if not (self.on_token_limit or self.on_max_rounds):
+            raise ValueError("extra round enabled with no trigger: set on_token_limit or "
+                             "on_max_rounds")
         return self
 
 
@@ -83,10 +85,12 @@ class LoopConfig(BaseModel):
 
     @model_validator(mode="after")
     def _check_parse_retry_abort_mutual_exclusion(self):
+        # a parse retry rolls the conversation back to before the failed turn, which would
+        # drop the partial output an abort/resume keeps; the two recovery paths cannot mix
         if self.max_parse_retries > 0 and self.max_aborts > 0:
-            raise ValueError(f"max_parse_retries ({self.max_parse_retries}) and max_aborts "
-                             f"({self.max_aborts}) cannot both be > 0: parse retry rollback does "
-                             "not handle abort partial state correctly")
+            raise ValueError(f"choose one recovery path: max_parse_retries={self.max_parse_retries} "
+                             f"and max_aborts={self.max_aborts} are both enabled, but a parse-retry "
+                             f"rollback would discard an aborted turn's partial output")
         return self
 
     @model_validator(mode="after")

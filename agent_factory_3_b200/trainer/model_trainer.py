@@ -14,8 +14,8 @@ What differs (B200 design):
     reduction is a single NCCL all-reduce (or reduce-scatter when the optimizer state is
     sharded) instead of per-parameter collectives;
   * loss/metric reductions are packed into one all-reduce;
-  * each rank takes its own buckets of the deterministic packing plan; the step's samples are
-    not broadcast as pickles over Gloo.
+  * rank 0 plans the step's packing and scatters to each rank only the samples of that rank's
+    buckets; no rank receives the whole step.
 """
 from __future__ import annotations
 
@@ -104,6 +104,7 @@ class ModelTrainer(RPCMixin):
                                                 vocab_size=self.model.cfg.vocab_size)
         self.step_count = 0
         self.last_step_events = None
+        self._outbox = None
         RPCMixin.__init__(self, group=rpc_group)
 
     # ------------------------------------------------------------------ setup
@@ -184,9 +185,7 @@ class ModelTrainer(RPCMixin):
         return out.loss_unscaled, states
 
     def _rank_microbatches(self, samples: list[TrainingSample]) -> list[list[int]]:
-        sampler = DeterministicPackedBatchSampler([len(s) for s in samples],
-                                                  max_capacity=self.config.max_capacity,
-                                                  world_size=self.world_size)
+        sampler = self._sampler([len(s) for s in samples])
         self._packing_stats = sampler.stats
         return sampler.plan_for_rank(self.rank)
 
@@ -231,29 +230,30 @@ class ModelTrainer(RPCMixin):
             metrics[k] = float((st.sum / st.count.clamp_min(1.0)).item())
         return metrics
 
-    @rpc_method(gather=False)
     def train_step(self, step_samples: list[TrainingSample]) -> dict[str, float]:
-        """One optimizer step over ``step_samples`` (all ranks receive the same list; each
-        trains on its buckets of the deterministic packing plan)."""
+        """One optimizer step over ``step_samples``.  Called on rank 0; the other ranks sit in
+        ``rpc_worker_loop``.  Rank 0 runs the deterministic packing plan over the whole list and
+        sends every rank only the samples of its own buckets (one scatter over the control
+        group: each rank receives its own payload, never the whole step); each rank collates
+        and trains its buckets, and the gradients meet in the data-parallel reduction."""
         if not step_samples:
             raise ValueError("train_step received empty step_samples")
         if any(s.divisor is None or s.divisor == 0 for s in step_samples):
             raise ValueError("train_step requires all samples to have a non-null, non-zero divisor.")
         t0 = time.perf_counter()
-        self.model.train()
-        plan = self._rank_microbatches(step_samples)
-        loss_sum = torch.zeros((), device=self.device)
-        states: dict[str, MeanMetricState] = {}
-        for idx in plan:
-            host = self.collator([step_samples[i] for i in idx])
-            batch = self._to_device(host)
-            loss, st = self._microbatch(batch)
-            loss.backward()
-            loss_sum = loss_sum + loss.detach()
-            for k, v in st.items():
-                states[k] = states[k].merge(v) if k in states else v
-        metrics = self._optimizer_step(loss_sum, states)
-        self.step_count += 1
+        sampler = self._sampler([len(s) for s in step_samples])
+        self._packing_stats = sampler.stats
+        outbox = []
+        for r in range(self.world_size):
+            mbs = sampler.plan_for_rank(r)
+            order = sorted({i for mb in mbs for i in mb})
+            local = {g: j for j, g in enumerate(order)}
+            outbox.append(([step_samples[i] for i in order], [[local[i] for i in mb] for mb in mbs]))
+        self._outbox = outbox
+        try:
+            metrics = self._train_own_buckets()
+        finally:
+            self._outbox = None
         dt = time.perf_counter() - t0
         seq = [len(s) for s in step_samples]
         comp = [s.num_loss_tokens() for s in step_samples]
@@ -263,6 +263,38 @@ class ModelTrainer(RPCMixin):
         metrics["train/seq_len_max"] = float(max(seq))
         metrics["train/completion_len_mean"] = sum(comp) / len(comp)
         metrics["train/completion_len_max"] = float(max(comp))
+        return metrics
+
+    def _sampler(self, lengths: list[int]) -> DeterministicPackedBatchSampler:
+        return DeterministicPackedBatchSampler(
+            lengths, max_capacity=self.config.max_capacity, world_size=self.world_size,
+            balance=self.config.packing_balance,
+            attention_tokens=self.config.packing_attention_tokens)
+
+    @rpc_method(gather=False)
+    def _train_own_buckets(self) -> dict[str, float]:
+        """Every rank: receive this rank's (samples, microbatch index lists) from rank 0,
+        then forward/backward each microbatch and take the optimizer step."""
+        if self._rpc_active():
+            box = [None]
+            dist.scatter_object_list(box, self._outbox if self.rank == 0 else None, src=0,
+                                     group=self._rpc_group)
+            samples, plan = box[0]
+        else:
+            samples, plan = self._outbox[0]
+        self.model.train()
+        loss_sum = torch.zeros((), device=self.device)
+        states: dict[str, MeanMetricState] = {}
+        for idx in plan:
+            host = self.collator([samples[i] for i in idx])
+            batch = self._to_device(host)
+            loss, st = self._microbatch(batch)
+            loss.backward()
+            loss_sum = loss_sum + loss.detach()
+            for k, v in st.items():
+                states[k] = states[k].merge(v) if k in states else v
+        metrics = self._optimizer_step(loss_sum, states)
+        self.step_count += 1
         return metrics
 
     def train_packed_batch(self, host_batch: dict) -> torch.Tensor:
@@ -380,6 +412,24 @@ class ModelTrainer(RPCMixin):
             torch.save(state, Path(output_dir) / f"training_state_rank{self.rank}.pt")
         elif self.rank == 0:
             torch.save(state, Path(output_dir) / "training_state.pt")
+
+    def training_state_layout(self, input_dir: str) -> str:
+        """"ok" when ``input_dir`` holds optimizer state in the layout this trainer loads
+        (per-rank files for the sharded optimizer, one file otherwise), "missing" when it has
+        none; raises when it only has the other layout (a sharded run resumed unsharded, or
+        the reverse), which would otherwise drop the AdamW moments without a word."""
+        d = Path(input_dir)
+        mine = d / (f"training_state_rank{self.rank}.pt" if self.sharded else "training_state.pt")
+        if mine.exists():
+            return "ok"
+        other = sorted(d.glob("training_state_rank*.pt")) if not self.sharded else \
+            ([d / "training_state.pt"] if (d / "training_state.pt").exists() else [])
+        if other:
+            raise ValueError(f"{d} holds {'sharded' if not self.sharded else 'replicated'} "
+                             f"optimizer state ({other[0].name}) but this trainer "
+                             f"{'shards' if self.sharded else 'does not shard'} its optimizer "
+                             f"state; resume with the same shard_optimizer_state and world size")
+        return "missing"
 
     @rpc_method(gather=False)
     def load_training_state(self, input_dir: str) -> None:

@@ -193,6 +193,22 @@ class RLFlow:
         write_meta(path, CheckpointMeta(step=step, batch_idx=batch_idx, factory_state=factory_state,
                                         wandb_run_id=run_id, weight_version=str(batch_idx)))
 
+    def _restore(self, path: Path) -> CheckpointMeta:
+        """Load a checkpoint written by ``_checkpoint``: adapter weights, then the optimizer
+        and scheduler state in whichever layout the trainer uses (one file, or one file per
+        rank for the sharded optimizer; every rank loads its own slice).  A checkpoint that
+        has optimizer state only in the other layout is an error, not a silent fresh start."""
+        from .checkpoint_utils import read_meta
+        meta = read_meta(path)
+        tr = self.model_trainer
+        tr.load_model(str(path))
+        kind = tr.training_state_layout(str(path))
+        if kind == "missing":
+            logger.warning("checkpoint %s has no optimizer state; AdamW restarts from zero", path)
+        else:
+            tr.load_training_state(str(path))
+        return meta
+
     def run(self, on_step: Callable[[dict, int], None] | None = None) -> list[dict]:
         tr = self.model_trainer
         tc = self.training_config
@@ -207,11 +223,7 @@ class RLFlow:
         factory_state = None
         run_id = None
         if resume is not None:
-            from .checkpoint_utils import read_meta
-            meta = read_meta(resume)
-            tr.load_model(str(resume))
-            if (resume / "training_state.pt").exists():
-                tr.load_training_state(str(resume))
+            meta = self._restore(resume)
             step_count, batch_idx = meta.step, meta.batch_idx
             factory_state, run_id = meta.factory_state, meta.wandb_run_id
         # initial weight sync (engines start from the trainer's weights / resumed adapter)

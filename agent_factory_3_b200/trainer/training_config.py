@@ -59,6 +59,10 @@ class TrainingConfig(BaseModel):
     # packing
     max_capacity: int = 20000
     pad_to_multiple_of_training: int = 1024
+    # rank balancing of the packing plan: "tokens" (the reference's rule) or "cost" (tokens
+    # plus the quadratic attention work, n + n^2 / packing_attention_tokens per sample)
+    packing_balance: Literal["tokens", "cost"] = "cost"
+    packing_attention_tokens: int = 32768
     dataloader_num_workers: int = 0
     # routing replay
     use_routing_replay: bool = True
@@ -88,7 +92,6 @@ class TrainingConfig(BaseModel):
     wandb_resume: bool = True
     # parallelism (B200 engine)
     shard_base_weights: bool = False          # True: FSDP-style per-layer all-gather of frozen base
-    shard_optimizer_state: bool = True        # ZeRO-1 style sharding of the trainable state
 
     @computed_field
     @property

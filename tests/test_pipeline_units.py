@@ -143,3 +143,42 @@ def test_metrics_saver_checkpoint_viewer(tmp_path):
     cu.write_meta(root / "checkpoint_latest", cu.CheckpointMeta(step=9, batch_idx=9))
     assert cu.resolve_resume_path("latest", root).name == "checkpoint_latest"
     assert [p.name for p in cu.cleanup_old_checkpoints(root, 1)] == ["checkpoint_step_1", "checkpoint_step_2"]
+
+
+def test_worker_lanes_bound_concurrency_and_report_failures(monkeypatch):
+    """A worker with 3 lanes never runs more than 3 rollouts at once, turns a raising rollout
+    into a failed result, answers every task exactly once and stops at the None marker
+    without taking the tasks queued behind it."""
+    import queue
+
+    from agent_factory_3_b200.orchestrator import worker as W
+    from agent_factory_3_b200.orchestrator.types import RolloutTask
+    from agent_factory_3_b200.rollout.parallel.config import RolloutConfig
+
+    state = {"active": 0, "peak": 0}
+
+    async def fake_rollout(cfg, url):
+        state["active"] += 1
+        state["peak"] = max(state["peak"], state["active"])
+        await asyncio.sleep(0.02)
+        state["active"] -= 1
+        if cfg.rollout_id == "t3":
+            raise RuntimeError("boom")
+        return _result(cfg.rollout_id)
+
+    monkeypatch.setattr(W, "execute_rollout", fake_rollout)
+    in_q, out_q = queue.Queue(), queue.Queue()
+    for i in range(8):
+        cfg = RolloutConfig(rollout_id=f"t{i}", user_prompt="p", loop_config=LoopConfig(),
+                            conv_config=ConversationConfig(), record_config=RecordConfig())
+        in_q.put(RolloutTask(config=cfg, server_url="http://x", group_id=f"g{i // 2}",
+                             index_in_group=i % 2))
+    in_q.put(None)
+    in_q.put("left for another worker")
+    asyncio.run(W._LaneWorker(in_q, out_q, 3, worker_id=0).run())
+    got = [out_q.get_nowait() for _ in range(8)]
+    assert out_q.empty() and state["peak"] == 3
+    assert in_q.get_nowait() == "left for another worker"
+    assert sorted((g, i) for g, i, _ in got) == sorted((f"g{i // 2}", i % 2) for i in range(8))
+    failed = [r for _, _, r in got if not r.success]
+    assert len(failed) == 1 and failed[0].rollout_id == "t3" and "boom" in failed[0].error

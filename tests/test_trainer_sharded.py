@@ -94,3 +94,63 @@ def test_sharded_optimizer_matches_replicated(tmp_path):
         assert roundtrip
     assert (tmp_path / "training_state_rank0.pt").exists()
     assert (tmp_path / "training_state_rank1.pt").exists()
+
+
+def _run_resume(rank, port, q, tmp):
+    """Sharded optimizer state saved and restored through RLFlow's checkpoint code."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    try:
+        from pathlib import Path
+
+        from agent_factory_3_b200.models.gpt_oss import GptOssConfig
+        from agent_factory_3_b200.orchestrator.types import per_rollout
+        from agent_factory_3_b200.rollout.config import LoopConfig
+        from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
+        from agent_factory_3_b200.trainer.rl_flow import RLFlow
+        from agent_factory_3_b200.trainer.training_config import TrainingConfig
+        mcfg = GptOssConfig.tiny()
+        cfg = TrainingConfig(model_id="tiny", lora_r=4, lora_alpha=8,
+                             lora_target_modules=["q_proj", "o_proj", "gate_up_proj", "down_proj"],
+                             random_init_seed=0, use_routing_replay=False, lr_warmup_steps=0,
+                             learning_rate=1e-2, max_capacity=256, pad_to_multiple_of_training=8,
+                             shard_optimizer_state=True, gradient_checkpointing=False,
+                             run_dir=os.path.join(tmp, "run"))
+        tr = ModelTrainer(cfg, model_config=mcfg, device="cpu")
+        ck = Path(tmp) / "ckpt"
+        if rank == 0:
+            flow = RLFlow(training_config=cfg, model_trainer=tr, dataset=[{"prompt": "x"}],
+                          reward_fn=per_rollout(lambda r, m: 0.0), server_urls=["http://unused"],
+                          loop_config=LoopConfig(), group_size=2, batch_size=2)
+            for _ in range(2):
+                tr.train_step(_samples(mcfg.vocab_size))
+            flow._checkpoint(ck, step=2, batch_idx=2, factory_state=None, run_id=None)
+            tr.reset_optimizer_state()
+            meta = flow._restore(ck)
+            assert meta.step == 2
+            tr.rpc_shutdown()
+        else:
+            tr.rpc_worker_loop()
+        saved = torch.load(ck / f"training_state_rank{rank}.pt", weights_only=False)
+        mine = tr.optimizer.state_dict()["state"]
+        ok = all(torch.equal(saved["optimizer"]["state"][k][n], v[n])
+                 for k, v in mine.items() for n in v if torch.is_tensor(v[n]) and v[n].dim() > 0)
+        nonzero = any(bool((v["exp_avg_sq"] != 0).any()) for v in mine.values())
+        q.put((rank, ok, nonzero, tr.step_count))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_optimizer_resume_through_rl_flow(tmp_path):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run_resume, args=(r, port, q, str(tmp_path))) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = sorted(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    for rank, ok, nonzero, steps in outs:
+        assert ok and nonzero, (rank, ok, nonzero)
+        assert steps == 2
