@@ -6,21 +6,34 @@
 // tensor core works on one tile while the other tile's softmax runs.
 //   warp 0      TMA: Q_A, Q_B once, then K_j (K-major) and V_j (MN-major, two 64-key boxes)
 //               into a 3-stage ring
-//   warp 1      tcgen05 issuer, in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1):
-//               S_X = Q_X K_j^T (M=128, N=128, K=64) into TMEM S[X]; O_X += P_X V_j (M=128,
-//               N=64, K=128) accumulated in TMEM O[X] across all key blocks, and the row sums
-//               l_X += P_X 1 (M=128, N=16, K=128 against a constant tile of ones) beside it
-//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: thread t owns query row t;
-//               reads S with tcgen05.ld, applies the causal / window / sequence masks, keeps a
-//               reference max m (log2 domain) that only moves when a block's max exceeds it by
-//               more than 2^8 (then O in TMEM and the row sum are rescaled once), writes
-//               P = 2^(s*scale*log2e - m) as bf16 into 128B-swizzled shared memory
+//   warp 1      tcgen05 issuer.  S_X(j+1) = Q_X K_{j+1}^T (M=128, N=128, K=64, both operands
+//               in shared memory) is issued as soon as the softmax of tile X has copied S_X(j)
+//               out of TMEM, i.e. while that softmax still runs; O_X += P_X(j) V_j (M=128,
+//               N=64, K=128) reads P straight from TMEM (A operand in tensor memory) and is
+//               issued when the softmax has stored P_X(j).
+//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: thread t owns query row t.
+//               It reads S with tcgen05.ld, applies the causal / window / sequence masks,
+//               keeps a reference max m (log2 domain) that only moves when a block's max
+//               exceeds it by more than 2^8 (then O in TMEM and the row sum are rescaled
+//               once), computes P = 2^(s*scale*log2e - m), adds P into a row sum held in
+//               registers and stores P as bf16 pairs into its TMEM lane (tcgen05.st).  The
+//               exponentials and row sums run as packed fp32x2 instructions; in blocks
+//               without masked entries a fixed share of the 2^x evaluations runs on the FMA
+//               pipe (cubic minimax polynomial after range reduction, relative error 7.5e-5,
+//               far below bf16's 2^-9) instead of the MUFU unit, which would otherwise bound
+//               the kernel: at head_dim 64 a 128x128 block needs 16384 exponentials against
+//               only 512 tensor-core clocks of MMA.
 //   The sink logit joins the denominator at the end: l += 2^(sink*log2e - m).
 //   Outputs: O (bf16) and the natural-log LSE per (head, query), sink included.
+//
+// TMEM columns: S[A] 0..127, S[B] 128..255, P[A] 256..319, P[B] 320..383 (bf16 pairs),
+//               O[A] 384..447, O[B] 448..511.
 //
 // Reference semantics: HF transformers eager_attention_forward for gpt-oss (sinks appended to
 // the logits, softmax, sink column dropped; models/gpt_oss in transformers); sliding window:
 // key j visible from query i iff i - j < window.
+#include <cstdlib>
+
 #include "common.h"
 #include "host_utils.h"
 #include "sm100.cuh"
@@ -35,15 +48,15 @@ constexpr int kKVStages = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;  // reference max moves only when exceeded by 2^8
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
+constexpr int kDefaultPoly = 6;
 
 struct AttnFwdSmem {
   // all tiles 1024-aligned
   static constexpr int Q = 0;                                  // 2 x 16 KB (A, B)
   static constexpr int K = Q + 2 * kBQ * kHD * 2;              // 3 x 16 KB
   static constexpr int V = K + kKVStages * kBKV * kHD * 2;     // 3 x 16 KB
-  static constexpr int P = V + kKVStages * kBKV * kHD * 2;     // 2 x 32 KB (A, B)
-  static constexpr int ONES = P + 2 * kBQ * kBKV * 2;          // 4 KB: bf16 ones [16 x 128]
-  static constexpr int BAR = ONES + 16 * kBKV * 2;
+  static constexpr int BAR = V + kKVStages * kBKV * kHD * 2;
   static constexpr int TOTAL = BAR + 1024;
 };
 
@@ -64,6 +77,56 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// ------------------------------ packed fp32x2 arithmetic --------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_of(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe.  x = n + f with n = rint(x) (adding 1.5 * 2^23 leaves n in
+// the low mantissa bits), f in [-0.5, 0.5]; 2^f by a cubic fitted to minimise the relative
+// error on that interval (Remez exchange, max relative error 7.5e-5); 2^n is added to the
+// exponent field.  x is clamped to >= -125 so the exponent cannot wrap; callers only pass
+// finite x <= 8 (unmasked blocks).
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x2, float& r0, float& r1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  const uint64_t xx = f2_pack(x0, x1);
+  const uint64_t t = f2_add(xx, f2_pack(kMagic, kMagic));
+  const uint64_t nf = f2_add(t, f2_pack(-kMagic, -kMagic));
+  const uint64_t fr = f2_fma(nf, f2_pack(-1.f, -1.f), xx);
+  uint64_t p = f2_fma(f2_pack(0.05517167f, 0.05517167f), fr, f2_pack(0.24261113f, 0.24261113f));
+  p = f2_fma(p, fr, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, fr, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
 // Key-block range of one 128-row query tile inside the CTA's span.
 struct FwdTile {
   int q0, q1;    // query rows [q0, q1); empty when q1 <= q0
@@ -80,25 +143,27 @@ __device__ __forceinline__ FwdTile fwd_tile(int q0, int q1, int seq0, int kv_lo,
   return t;
 }
 
-// MMA-issuer state of one tile (kept in registers: the tile index is a template argument).
+// MMA-issuer state of one tile.
 struct FwdIssue {
-  int jlo, jhi;  // key blocks of the tile
-  int n_s, n_pv; // S / PV blocks issued so far
+  int jlo, jhi;   // key blocks of the tile
+  int n_s, n_pv;  // S / PV blocks issued so far
 };
 
+// S_X(j) = Q_X K_j^T into TMEM S[X].  The S buffer must have been read by the softmax of the
+// tile's previous block (s_free).
 template <int X>
 __device__ __forceinline__ bool fwd_issue_s(FwdIssue& t, int j, uint32_t tmem, uint32_t sq,
-                                            uint32_t sk0, uint64_t* s_empty, uint64_t* s_full,
+                                            uint32_t sk0, uint64_t* s_free, uint64_t* s_full,
                                             int* err, volatile int* abort_flag) {
   if (j < t.jlo || j >= t.jhi) return true;
-  if (!mbar_wait(&s_empty[X], (t.n_s & 1) ^ 1, err, abort_flag)) return false;
+  if (t.n_s > 0 && !mbar_wait(&s_free[X], (t.n_s - 1) & 1, err, abort_flag)) return false;
   tc_fence_after();
   constexpr uint32_t idesc_s = make_idesc_bf16(kBQ, kBKV, false, false);
   const uint32_t q = sq + X * kBQ * kHD * 2;
   const uint32_t k = sk0 + (j % kKVStages) * kBKV * kHD * 2;
 #pragma unroll
   for (int kk = 0; kk < kHD / 16; ++kk) {
-    umma_f16(tmem + X * kBKV, make_smem_desc(q + kk * 32, 16, 1024, kLayoutSW128),
+    umma_f16(tmem + kColS + X * kBKV, make_smem_desc(q + kk * 32, 16, 1024, kLayoutSW128),
              make_smem_desc(k + kk * 32, 16, 1024, kLayoutSW128), idesc_s, kk > 0);
   }
   umma_commit(&s_full[X]);
@@ -106,36 +171,31 @@ __device__ __forceinline__ bool fwd_issue_s(FwdIssue& t, int j, uint32_t tmem, u
   return true;
 }
 
+// O_X += P_X(j) V_j with P read from TMEM (two bf16 per column, row = lane).
 template <int X>
-__device__ __forceinline__ bool fwd_issue_pv(FwdIssue& t, int j, uint32_t tmem, uint32_t sp0,
-                                             uint32_t sv0, uint64_t* p_full, uint64_t* o_done,
-                                             int* err, volatile int* abort_flag) {
+__device__ __forceinline__ bool fwd_issue_pv(FwdIssue& t, int j, uint32_t tmem, uint32_t sv0,
+                                             uint64_t* p_full, uint64_t* o_ready, int* err,
+                                             volatile int* abort_flag) {
   if (j < t.jlo || j >= t.jhi) return true;
   if (!mbar_wait(&p_full[X], t.n_pv & 1, err, abort_flag)) return false;
   tc_fence_after();
   constexpr uint32_t idesc_o = make_idesc_bf16(kBQ, kHD, false, true);
-  constexpr uint32_t idesc_l = make_idesc_bf16(kBQ, 16, false, false);
-  const uint32_t pp = sp0 + X * kBQ * kBKV * 2;
-  const uint32_t ones = sp0 + 2 * kBQ * kBKV * 2;
   const uint32_t v = sv0 + (j % kKVStages) * kBKV * kHD * 2;
   const uint32_t first = t.n_pv > 0 ? 1u : 0u;
 #pragma unroll
   for (int kk = 0; kk < kBKV / 16; ++kk) {
-    const uint64_t ad = make_smem_desc(pp + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
     const uint64_t bd = make_smem_desc(v + (kk / 4) * 8192 + (kk % 4) * 2048, 8192, 1024, kLayoutSW128);
-    umma_f16(tmem + 256 + X * kHD, ad, bd, idesc_o, kk > 0 ? 1u : first);
+    umma_f16_tmem_a(tmem + kColO + X * kHD, tmem + kColP + X * 64 + kk * 8, bd, idesc_o,
+                    kk > 0 ? 1u : first);
   }
-#pragma unroll
-  for (int kk = 0; kk < kBKV / 16; ++kk) {  // row sums of P: P x ones[16 x 128]^T
-    const uint64_t ad = make_smem_desc(pp + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
-    const uint64_t bd = make_smem_desc(ones + (kk / 4) * 2048 + (kk % 4) * 32, 16, 1024, kLayoutSW128);
-    umma_f16(tmem + 384 + X * 16, ad, bd, idesc_l, kk > 0 ? 1u : first);
-  }
-  umma_commit(&o_done[X]);
+  umma_commit(&o_ready[X]);
   ++t.n_pv;
   return true;
 }
 
+// POLY: number of the sixteen 8-column groups of a 128-key block whose exponentials run on
+// the FMA pipe in unmasked blocks (0 = all on the MUFU unit).
+template <int POLY>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qk,
                     const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
@@ -146,10 +206,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;    // [3]
   uint64_t* kv_empty = bars + 4;   // [3]
-  uint64_t* s_full = bars + 7;     // [2] per tile
-  uint64_t* s_empty = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;    // [2]
-  uint64_t* o_done = bars + 13;    // [2]
+  uint64_t* s_full = bars + 7;     // [2] per tile: S in TMEM
+  uint64_t* s_free = bars + 9;     // [2] S copied out of TMEM by the softmax
+  uint64_t* p_full = bars + 11;    // [2] P stored in TMEM (O rescaled if needed)
+  uint64_t* o_ready = bars + 13;   // [2] PV complete: P buffer free, O stable
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -177,9 +237,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
-      mbar_init(&s_empty[x], 128);
-      mbar_init(&p_full[x], 128);
-      mbar_init(&o_done[x], 1);
+      mbar_init(&s_free[x], 4);    // one arrive per softmax warp
+      mbar_init(&p_full[x], 4);
+      mbar_init(&o_ready[x], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -188,16 +248,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
-  for (int i = threadIdx.x; i < 16 * kBKV * 2 / 16; i += blockDim.x)  // bf16 1.0 = 0x3F80
-    st_shared_v4(smem_u32(smem + AttnFwdSmem::ONES) + i * 16, 0x3F803F80u, 0x3F803F80u,
-                 0x3F803F80u, 0x3F803F80u);
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  // TMEM columns: S[A] 0..127, S[B] 128..255, O[A] 256..319, O[B] 320..383,
-  //               l[A] 384..399, l[B] 400..415 (16 equal columns each)
 
   // register split (launch: 384 x 168): control warps 128 x 96 + softmax 256 x 200 = 63488 <= 64512
   if (warp < 4) {
@@ -224,22 +278,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t sq = smem_u32(smem + AttnFwdSmem::Q);
         const uint32_t sk0 = smem_u32(smem + AttnFwdSmem::K);
         const uint32_t sv0 = smem_u32(smem + AttnFwdSmem::V);
-        const uint32_t sp0 = smem_u32(smem + AttnFwdSmem::P);
         FwdIssue a{tl[0].jlo, tl[0].jhi, 0, 0}, b{tl[1].jlo, tl[1].jhi, 0, 0};
         bool ok = mbar_wait(q_full, 0, p.err, abort_flag) &&
                   mbar_wait(&kv_full[0], 0, p.err, abort_flag);
-        ok = ok && fwd_issue_s<0>(a, 0, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag) &&
-             fwd_issue_s<1>(b, 0, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
+        ok = ok && fwd_issue_s<0>(a, 0, tmem, sq, sk0, s_free, s_full, p.err, abort_flag) &&
+             fwd_issue_s<1>(b, 0, tmem, sq, sk0, s_free, s_full, p.err, abort_flag);
         for (int j = 0; ok && j < nb; ++j) {
-          ok = fwd_issue_pv<0>(a, j, tmem, sp0, sv0, p_full, o_done, p.err, abort_flag);
-          if (ok && j + 1 < nb) {
+          const bool next = j + 1 < nb;
+          if (next)
             ok = mbar_wait(&kv_full[(j + 1) % kKVStages], ((j + 1) / kKVStages) & 1, p.err,
-                           abort_flag) &&
-                 fwd_issue_s<0>(a, j + 1, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
-          }
-          ok = ok && fwd_issue_pv<1>(b, j, tmem, sp0, sv0, p_full, o_done, p.err, abort_flag);
-          if (ok && j + 1 < nb)
-            ok = fwd_issue_s<1>(b, j + 1, tmem, sq, sk0, s_empty, s_full, p.err, abort_flag);
+                           abort_flag);
+          // S of the next block runs while the softmax of this block is still working
+          if (ok && next)
+            ok = fwd_issue_s<0>(a, j + 1, tmem, sq, sk0, s_free, s_full, p.err, abort_flag);
+          ok = ok && fwd_issue_pv<0>(a, j, tmem, sv0, p_full, o_ready, p.err, abort_flag);
+          if (ok && next)
+            ok = fwd_issue_s<1>(b, j + 1, tmem, sq, sk0, s_free, s_full, p.err, abort_flag);
+          ok = ok && fwd_issue_pv<1>(b, j, tmem, sv0, p_full, o_ready, p.err, abort_flag);
           umma_commit(&kv_empty[j % kKVStages]);
         }
       }
@@ -252,11 +307,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int row = q * 32 + lane;
     const int qi = t.q0 + row;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + x * kBKV;
-    const uint32_t o_addr = tmem + lane_base + 256 + x * kHD;
-    const uint32_t l_addr = tmem + lane_base + 384 + x * 16;
-    const uint32_t prow = smem_u32(smem + AttnFwdSmem::P + x * kBQ * kBKV * 2 + row * 128);
+    const uint32_t s_addr = tmem + lane_base + kColS + x * kBKV;
+    const uint32_t p_addr = tmem + lane_base + kColP + x * 64;
+    const uint32_t o_addr = tmem + lane_base + kColO + x * kHD;
+    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
     float m_ref = -INFINITY;
+    float l_run = 0.f;  // row sum of P relative to m_ref
     int c = 0;
     bool ok = true;
     for (int j = t.jlo; j < t.jhi; ++j, ++c) {
@@ -279,7 +335,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&s_empty[x]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);   // the MMA may overwrite S with block j+1
       const int k0 = kv_lo + j * kBKV;
       const bool need_mask = (k0 + kBKV - 1 > t.q0) || (k0 < seq0) ||
                              (p.window > 0 && t.q0 + kBQ - 1 - k0 >= p.window);
@@ -309,44 +366,69 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         m_ref = cand;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // S(j) was issued after PV(j-1) by the same thread and its commit covers every earlier
-      // MMA, so PV(j-1) is complete here: the P buffer is free and O is stable.
+      const uint64_t negm2 = f2_pack(-m_use, -m_use);
+      // P = 2^(s * scale - m) as bf16 pairs; the row sum accumulates in two packed lanes
+      uint32_t pk[kBKV / 2];
+      uint64_t rs2 = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int c8 = 0; c8 < kBKV / 8; ++c8) {
-        float pv[8];
+        const bool poly = POLY > 0 && ((c8 * POLY) % 16) < POLY;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pv[e] = ex2(fmaf(sv[c8 * 8 + e], p.scale_log2, -m_use));
-        const int blk = c8 >> 3, ch = (c8 & 7) ^ (row & 7);
-        st_shared_v4(prow + blk * 16384 + ch * 16, pack_bf16x2(pv[0], pv[1]),
-                     pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
-                     pack_bf16x2(pv[6], pv[7]));
-      }
-      if (c > 0 && __any_sync(0xffffffffu, resc)) {  // rescale O and l before PV(j) adds
-#pragma unroll
-        for (int h32 = 0; h32 < kHD / 32; ++h32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(o_addr + h32 * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-          tmem_st_32x32b_x32(o_addr + h32 * 32, r);
+        for (int e = 0; e < 8; e += 2) {
+          const uint64_t x2 = f2_fma(f2_pack(sv[c8 * 8 + e], sv[c8 * 8 + e + 1]), scale2, negm2);
+          float e0, e1;
+          if (poly && !need_mask) {
+            exp2_poly_x2(x2, e0, e1);
+          } else {
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            e0 = ex2(x0);
+            e1 = ex2(x1);
+          }
+          rs2 = f2_add(rs2, f2_pack(e0, e1));
+          pk[c8 * 4 + e / 2] = bf16x2_of(e0, e1);
         }
-        const uint32_t lv = tmem_ld_32x32b_x1(l_addr);
-        tmem_ld_wait();
-        tmem_st_32x32b_x1(l_addr, __float_as_uint(__uint_as_float(lv) * alpha));
-        tmem_st_wait();
       }
-      fence_proxy_async_smem();
+      float rs0, rs1;
+      f2_unpack(rs2, rs0, rs1);
+      l_run = l_run * alpha + (rs0 + rs1);
+      // PV of the previous block must be complete before P is overwritten or O rescaled
+      if (c > 0) {
+        if (!mbar_wait(&o_ready[x], (c - 1) & 1, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+          for (int h32 = 0; h32 < kHD / 32; ++h32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_addr + h32 * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st_32x32b_x32(o_addr + h32 * 32, r);
+          }
+        }
+      }
+      {
+        uint32_t w0[32], w1[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          w0[e] = pk[e];
+          w1[e] = pk[32 + e];
+        }
+        tmem_st_32x32b_x32(p_addr, w0);
+        tmem_st_32x32b_x32(p_addr + 32, w1);
+      }
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[x]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
     }
     if (ok && c > 0) {
-      if (mbar_wait(&o_done[x], (c - 1) & 1, p.err, abort_flag)) {
+      if (mbar_wait(&o_ready[x], (c - 1) & 1, p.err, abort_flag)) {
         tc_fence_after();
         uint32_t o0[32], o1[32];
         tmem_ld_32x32b_x32(o_addr, o0);
         tmem_ld_32x32b_x32(o_addr + 32, o1);
-        const float l_run = __uint_as_float(tmem_ld_32x32b_x1(l_addr));
         tmem_ld_wait();
         if (qi < t.q1) {
           // the sink joins the max: a row whose scores all lie far below the sink would
@@ -422,16 +504,23 @@ void attn_fwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor tiles, torch
   p.scale_log2 = (float)scale * kLog2e;
   p.err = device_error_ptr();
   const int smem = AttnFwdSmem::TOTAL + 1024;
-  static bool attr[64] = {};
+  // share of the exponentials on the FMA pipe (8-column groups out of 16), AF3_ATTN_POLY
+  static const int poly = [] {
+    const char* e = std::getenv("AF3_ATTN_POLY");
+    const int v = e ? std::atoi(e) : kDefaultPoly;
+    return (v == 0 || v == 2 || v == 4 || v == 6 || v == 8) ? v : kDefaultPoly;
+  }();
+  static bool attr[64][5] = {};
   int dev;
   AF3_CUDA_CHECK(cudaGetDevice(&dev));
-  if (!attr[dev]) {
-    AF3_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr[dev] = true;
+  auto kern = poly == 0 ? attn_fwd_kernel<0> : poly == 2 ? attn_fwd_kernel<2> :
+              poly == 4 ? attn_fwd_kernel<4> : poly == 6 ? attn_fwd_kernel<6> : attn_fwd_kernel<8>;
+  if (!attr[dev][poly / 2]) {
+    AF3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr[dev][poly / 2] = true;
   }
   dim3 grid((unsigned)hq, (unsigned)n_tiles);
-  attn_fwd_kernel<<<grid, kFwdThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, p);
+  kern<<<grid, kFwdThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, p);
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 

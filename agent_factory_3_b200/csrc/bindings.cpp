@@ -16,11 +16,14 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           int64_t band, int64_t out_group_stride, int64_t max_ctas,
           c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2);
 void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
+void mxfp4_dequant_gather(torch::Tensor block_ptrs, torch::Tensor scale_ptrs,
+                          int64_t experts_per_rank, torch::Tensor out);
 void peer_cast_copy(int64_t dst_ptr, int64_t dst_numel, std::vector<torch::Tensor> srcs,
                     std::vector<int64_t> offsets);
 std::tuple<torch::Tensor, pybind11::bytes> symm_alloc(int64_t nbytes, int64_t device);
 int64_t ipc_open(pybind11::bytes handle);
 void ipc_close(int64_t ptr);
+void copy_from_address(int64_t src, torch::Tensor dst);
 void enable_peer_access(int64_t peer);
 void tp_allreduce_norm(std::vector<int64_t> bufs, std::vector<int64_t> flags, int64_t rank,
                        int64_t epoch, int64_t ld_buf, c10::optional<torch::Tensor> residual,
@@ -85,11 +88,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"),
         py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("K2") = 0);
   m.def("mxfp4_dequant", &af3::mxfp4_dequant);
+  m.def("mxfp4_dequant_gather", &af3::mxfp4_dequant_gather,
+        "MXFP4 -> bf16 of an expert stack sharded over peer-mapped per-rank buffers");
   m.def("peer_cast_copy", &af3::peer_cast_copy,
         "cast fp32/bf16 tensors to bf16 and store them into a (peer) staging buffer");
   m.def("symm_alloc", &af3::symm_alloc, "zeroed cudaMalloc buffer + its CUDA IPC handle");
   m.def("ipc_open", &af3::ipc_open, "map another process's IPC buffer; returns a device pointer");
   m.def("ipc_close", &af3::ipc_close);
+  m.def("copy_from_address", &af3::copy_from_address,
+        "copy dst.nbytes() bytes from a device address (own or peer-mapped) into dst");
   m.def("enable_peer_access", &af3::enable_peer_access,
         "allow kernels on the current device to access device `peer` (same process)");
   m.def("tp_allreduce_norm", &af3::tp_allreduce_norm,

@@ -53,6 +53,56 @@ void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out
   AF3_CUDA_CHECK(cudaGetLastError());
 }
 
+// MXFP4 -> bf16 of an expert stack whose experts are spread over the ranks of a node: expert e
+// lives on rank e / experts_per_rank at local index e % experts_per_rank, in that rank's
+// peer-mapped shard (plain loads over NVLink for the other ranks' experts, no TMA).  This is
+// the all-gather of the sharded frozen experts fused with their dequantisation: the packed
+// bytes cross NVLink once and only the bf16 result is written, to this GPU's own memory.
+// Grid: (blocks over the words of one expert, experts).
+__global__ void mxfp4_dequant_gather_kernel(const uint64_t* __restrict__ block_ptrs,
+                                            const uint64_t* __restrict__ scale_ptrs,
+                                            int experts_per_rank, int64_t words_per_expert,
+                                            uint4* __restrict__ out) {
+  const int e = blockIdx.y;
+  const int r = e / experts_per_rank, le = e - r * experts_per_rank;
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(block_ptrs[r]) + le * words_per_expert;
+  const uint8_t* scales = reinterpret_cast<const uint8_t*>(scale_ptrs[r]) + le * (words_per_expert / 4);
+  uint4* dst = out + (int64_t)e * words_per_expert;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words_per_expert;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = __ldg(words + i);
+    const uint32_t s = __ldg(scales + (i >> 2));
+    dst[i] = e2m1x8_to_bf16x8(w, e8m0_to_bf16_bits(s));
+  }
+}
+
+void mxfp4_dequant_gather(torch::Tensor block_ptrs, torch::Tensor scale_ptrs,
+                          int64_t experts_per_rank, torch::Tensor out) {
+  AF3_CHECK(block_ptrs.is_cuda() && block_ptrs.scalar_type() == torch::kInt64 &&
+                scale_ptrs.is_cuda() && scale_ptrs.scalar_type() == torch::kInt64,
+            "pointer tables must be int64 CUDA tensors");
+  AF3_CHECK(block_ptrs.numel() == scale_ptrs.numel() && block_ptrs.numel() >= 1, "pointer tables");
+  AF3_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.is_contiguous() &&
+                out.dim() == 3, "out must be contiguous bf16 [E, N, K]");
+  AF3_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out must be 16-byte aligned");
+  const int64_t E = out.size(0), N = out.size(1), K = out.size(2);
+  AF3_CHECK(K % 32 == 0, "K must be a multiple of 32");
+  AF3_CHECK(experts_per_rank > 0 && E == experts_per_rank * block_ptrs.numel(),
+            "experts must equal experts_per_rank x ranks");
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int64_t words = N * K / 8;   // one 32-bit word = 8 e2m1 values
+  if (E == 0 || words == 0) return;
+  const int threads = 256;
+  const int64_t per = std::max<int64_t>(1, std::min<int64_t>((words + threads - 1) / threads,
+                                                              (int64_t)num_sms() * 32 / E + 1));
+  mxfp4_dequant_gather_kernel<<<dim3((unsigned)per, (unsigned)E), threads, 0,
+                                at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint64_t*>(block_ptrs.data_ptr<int64_t>()),
+      reinterpret_cast<const uint64_t*>(scale_ptrs.data_ptr<int64_t>()), (int)experts_per_rank,
+      words, reinterpret_cast<uint4*>(out.data_ptr()));
+  AF3_CUDA_CHECK(cudaGetLastError());
+}
+
 // ------------------------------------ router -----------------------------------------
 // One warp per token.  If `replay`, ids[t, :] are read; otherwise the top-K logits are
 // selected (ties: lower expert id first, as torch.topk on CPU/CUDA for distinct values).

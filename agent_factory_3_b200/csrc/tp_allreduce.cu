@@ -212,6 +212,17 @@ void ipc_close(int64_t ptr) {
   AF3_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
 }
 
+// dst (contiguous, current device) <- dst.nbytes() bytes at device address src (this GPU's
+// memory or a peer mapping), one async copy on the current stream.
+void copy_from_address(int64_t src, torch::Tensor dst) {
+  AF3_CHECK(dst.is_cuda() && dst.is_contiguous(), "copy_from_address: dst must be contiguous CUDA");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  const size_t n = dst.numel() * dst.element_size();
+  if (n == 0) return;
+  AF3_CUDA_CHECK(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src), n,
+                                 cudaMemcpyDefault, at::cuda::getCurrentCUDAStream()));
+}
+
 // x = residual + sum over ranks of the partials at bufs[j] (+ byte offset), and, with w,
 // xn = RMSNorm(x) * w.  bufs / flags: one device address per rank (own + peer mappings).
 void tp_allreduce_norm(std::vector<int64_t> bufs, std::vector<int64_t> flags, int64_t rank,

@@ -343,8 +343,11 @@ class Engine:
     def _spec_ok(self, r: Request) -> bool:
         return (self.drafter is not None and r.top_k <= 0 and r.top_p >= 1.0 and r.min_p <= 0)
 
-    def _append(self, r: Request, t: int, lp: float, ent: float) -> bool:
-        """Record one generated token; returns True when the request has finished."""
+    def _append(self, r: Request, t: int, lp: float, ent: float, top=None) -> bool:
+        """Record one generated token (``top``: its top-k alternatives, when computed);
+        returns True when the request has finished."""
+        if r.return_logprob and r.top_logprobs_num > 0:
+            r.output_top.append(top if top is not None else [(float(lp), int(t))])
         r.output_ids.append(int(t))
         r.output_logprobs.append(float(lp))
         r.output_entropy.append(float(ent))
@@ -418,15 +421,17 @@ class Engine:
             if spec_reqs:
                 logits = logits.index_select(0, torch.tensor([out.logit_offsets[i] for i in plain],
                                                              device=dev, dtype=torch.long))
+            raw = logits
             if any(r.top_k > 0 or r.top_p < 1.0 for r in sample_owners):
                 logits = _apply_top_k_top_p(logits, sample_owners)
             steps = [len(r.output_ids) for r in sample_owners]
             tok, lp, ent = D.sample(logits, temps, seeds + torch.tensor(steps, device=dev) * 1000003,
                                     self.step_count, minp if float(minp.max()) > 0 else None)
+            tops = _top_logprobs(raw, temps, sample_owners)
             tok, lp, ent = tok.tolist(), lp.tolist(), ent.tolist()
             self.gen_tokens_window.append((time.time(), len(tok)))
-            for r, t, l, e in zip(sample_owners, tok, lp, ent):
-                self._append(r, t, l, e)
+            for j, (r, t, l, e) in enumerate(zip(sample_owners, tok, lp, ent)):
+                self._append(r, t, l, e, tops.get(j))
                 if r.stream and r.finish_reason is None:
                     self._emit(r, final=False)
         if spec_reqs:
@@ -471,7 +476,11 @@ class Engine:
         if r.return_logprob:
             meta["output_token_logprobs"] = [[lp, t, None] for lp, t in zip(r.output_logprobs, r.output_ids)]
             if r.top_logprobs_num:
-                meta["output_top_logprobs"] = [[[lp, t, None]] for lp, t in zip(r.output_logprobs, r.output_ids)]
+                # per generated token: its top-k alternatives [logprob, token_id, None] under
+                # the request's temperature (tokens accepted by speculative verification carry
+                # only themselves)
+                meta["output_top_logprobs"] = [[[float(v), int(t), None] for v, t in row]
+                                               for row in r.output_top]
         if r.return_entropy:
             meta["output_token_entropy"] = list(r.output_entropy)
         if final and r.return_routed_experts and r.pages:
@@ -524,6 +533,23 @@ def _load_lora_into(model, sd: dict) -> None:
                 E, a, b = p.shape
                 t = t.reshape(E, a, b) if ab == "A" else t.reshape(a, E, b).permute(1, 0, 2)
                 p.copy_(t.to(p.device, p.dtype))
+
+
+def _top_logprobs(logits: torch.Tensor, temps: torch.Tensor, owners: list) -> dict:
+    """{row: [(logprob, token), ...]} -- the top ``top_logprobs_num`` tokens of every row whose
+    request asked for them, log-softmax under the request's temperature (greedy rows use 1)."""
+    rows = [j for j, r in enumerate(owners) if r.return_logprob and r.top_logprobs_num > 0]
+    if not rows:
+        return {}
+    k = max(owners[j].top_logprobs_num for j in rows)
+    idx = torch.tensor(rows, device=logits.device, dtype=torch.long)
+    t = temps.index_select(0, idx).float()
+    t = torch.where(t > 0, t, torch.ones_like(t))
+    lp = torch.log_softmax(logits.index_select(0, idx).float() / t[:, None], dim=-1)
+    vals, ids = lp.topk(min(k, lp.shape[-1]), dim=-1)
+    vals, ids = vals.tolist(), ids.tolist()
+    return {j: list(zip(vals[n][:owners[j].top_logprobs_num], ids[n][:owners[j].top_logprobs_num]))
+            for n, j in enumerate(rows)}
 
 
 def _apply_top_k_top_p(logits: torch.Tensor, reqs: list[Request]) -> torch.Tensor:

@@ -48,10 +48,12 @@ def hf_state_dict(model: GptOssForCausalLM, include_experts: bool = True) -> dic
         sd[p + "mlp.router.weight"] = m.router_weight.detach()
         sd[p + "mlp.router.bias"] = m.router_bias.detach().to(torch.bfloat16)
         if include_experts:
-            sd[p + "mlp.experts.gate_up_proj_blocks"] = m.gate_up_blocks
-            sd[p + "mlp.experts.gate_up_proj_scales"] = m.gate_up_scales
-            sd[p + "mlp.experts.down_proj_blocks"] = m.down_blocks
-            sd[p + "mlp.experts.down_proj_scales"] = m.down_scales
+            sh = getattr(m, "expert_shards", None)     # sharded base: gather every rank's experts
+            full = (lambda key, t: sh.packed(key, t)) if sh is not None else (lambda key, t: t)
+            sd[p + "mlp.experts.gate_up_proj_blocks"] = full("gu_blocks", m.gate_up_blocks)
+            sd[p + "mlp.experts.gate_up_proj_scales"] = full("gu_scales", m.gate_up_scales)
+            sd[p + "mlp.experts.down_proj_blocks"] = full("dn_blocks", m.down_blocks)
+            sd[p + "mlp.experts.down_proj_scales"] = full("dn_scales", m.down_scales)
         sd[p + "mlp.experts.gate_up_proj_bias"] = m.gate_up_bias.detach().to(torch.bfloat16)
         sd[p + "mlp.experts.down_proj_bias"] = m.down_bias.detach().to(torch.bfloat16)
     return sd
@@ -190,8 +192,9 @@ def merged_state_dict(model: GptOssForCausalLM, dtype=torch.bfloat16,
             w = w + s * (a.lora["o_proj_B"].float() @ a.lora["o_proj_A"].float())
         out[p + "self_attn.o_proj.weight"] = w.to(dtype)
         if not attention_only:
-            gu = mxfp4.dequantize(m.gate_up_blocks, m.gate_up_scales).float()
-            dn = mxfp4.dequantize(m.down_blocks, m.down_scales).float()
+            ex = m.experts()        # gathers the stacks when the base is sharded
+            gu = ex.gate_up().float()
+            dn = ex.down().float()
             if "gu_A" in m.lora:
                 gu = gu + m.lora_scaling * torch.bmm(m.lora["gu_B"].float(), m.lora["gu_A"].float())
             if "dn_A" in m.lora:

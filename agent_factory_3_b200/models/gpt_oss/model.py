@@ -22,7 +22,7 @@ import torch.nn as nn
 import torch.utils.checkpoint as ckpt
 
 from ...ops import mxfp4
-from ...ops.attention import AttentionPlan, attention
+from ...ops.attention import AttentionOutputCache, AttentionPlan, attention
 from ...ops.linear import block_diag_b, lora_linear
 from ...ops.logprob import linear_logprob_entropy
 from ...ops.moe_layer import ExpertWeights, moe_forward
@@ -57,6 +57,7 @@ class GptOssAttention(nn.Module):
         self.cfg = cfg
         self.layer = layer
         self.window = cfg.window(layer)
+        self.layer_idx = layer
         H, D = cfg.hidden_size, cfg.head_dim
         self.qkv_weight = nn.Parameter(torch.empty(cfg.qkv_size, H, device=device, dtype=dtype),
                                        requires_grad=False)
@@ -104,8 +105,10 @@ class GptOssAttention(nn.Module):
         qkv = lora_linear(xn, self.qkv_weight, self.qkv_bias, A, B, None, self.lora_scaling)
         qkv = _RopeFn.apply(qkv, cfg.num_attention_heads + cfg.num_key_value_heads,
                             cfg.head_dim, pos, cos, sin)
+        # full-attention layers may hand their output to the checkpoint recompute
         o = attention(qkv, self.sinks, cu_seqlens, cfg.num_attention_heads,
-                      cfg.num_key_value_heads, cfg.head_dim, self.window, None, plan)
+                      cfg.num_key_value_heads, cfg.head_dim, self.window, None, plan,
+                      cache_key=self.layer_idx if self.window == 0 else None)
         oA = self.lora["o_proj_A"] if "o_proj_A" in self.lora else None
         oB = self.lora["o_proj_B"] if "o_proj_B" in self.lora else None
         return lora_linear(o, self.o_weight, self.o_bias, oA, oB, residual, self.lora_scaling)
@@ -140,7 +143,8 @@ class GptOssMoE(nn.Module):
 
     def experts(self) -> ExpertWeights:
         return ExpertWeights(self.gate_up_blocks, self.gate_up_scales, self.gate_up_bias,
-                             self.down_blocks, self.down_scales, self.down_bias)
+                             self.down_blocks, self.down_scales, self.down_bias,
+                             shards=getattr(self, "expert_shards", None))
 
     def forward(self, xn, residual, replay_ids=None, routing_out=None):
         cfg = self.cfg
@@ -183,6 +187,8 @@ class GptOssForCausalLM(nn.Module):
         self.lm_head = nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size, device=device,
                                                 dtype=dtype), requires_grad=False)
         self.gradient_checkpointing = True
+        # bytes of full-attention outputs kept for the checkpoint recompute (0 = recompute all)
+        self.attention_cache_bytes = 0
         self._rope_cache = None
 
     # ------------------------------------------------------------------ init / params
@@ -286,6 +292,9 @@ class GptOssForCausalLM(nn.Module):
         cu = cu_seqlens.to(device=dev, dtype=torch.int32)
         if plan is None and dev.type == "cuda":
             plan = AttentionPlan(cu_seqlens, dev)
+            if (self.gradient_checkpointing and torch.is_grad_enabled() and not record_routing
+                    and self.attention_cache_bytes > 0):
+                plan.cache = AttentionOutputCache(self.attention_cache_bytes)
         x = self.embed(input_ids)
         if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
             x = x.detach().requires_grad_(True)  # checkpoint segments need a grad-carrying input

@@ -78,13 +78,52 @@ class _AttentionRef(torch.autograd.Function):
         return gx.to(qkv.dtype), gs.to(sinks.dtype), None, None, None, None, None, None
 
 
+class AttentionOutputCache:
+    """Attention outputs kept from a checkpointed layer's first forward for its recompute.
+
+    Activation checkpointing runs each decoder layer's forward twice.  For full-attention
+    layers over long packed sequences the attention kernel dominates that recompute, while
+    its result -- O [T, Hq*64] bf16 plus the LSE [Hq, T] fp32 the backward needs anyway -- is
+    small next to what checkpointing saves.  Up to ``budget_bytes`` of such results are kept
+    (first come, first kept) and handed to the recompute, which then skips the kernel.  Each
+    entry is released when the recompute takes it, so its memory lives from the layer's
+    forward to the start of the layer's backward."""
+
+    def __init__(self, budget_bytes: int):
+        self.budget = int(budget_bytes)
+        self.used = 0
+        self.entries: dict = {}
+        self.hits = 0
+
+    def take(self, key):
+        e = self.entries.pop(key, None)
+        if e is not None:
+            self.used -= e[0].numel() * e[0].element_size() + e[1].numel() * 4
+            self.hits += 1
+        return e
+
+    def offer(self, key, out, lse) -> None:
+        n = out.numel() * out.element_size() + lse.numel() * 4
+        if key is None or key in self.entries or self.used + n > self.budget:
+            return
+        self.entries[key] = (out, lse)
+        self.used += n
+
+
 class _AttentionKernel(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, sinks, cu_seqlens, hq, hkv, d, window, scale, plan):
-        out = torch.empty(qkv.shape[0], hq * d, device=qkv.device, dtype=qkv.dtype)
-        lse = torch.empty(hq, qkv.shape[0], device=qkv.device, dtype=torch.float32)
-        ext().attn_fwd(qkv, sinks.float().contiguous(), plan.tiles, plan.cu, out, lse, hq, hkv,
-                       d, window, scale)
+    def forward(ctx, qkv, sinks, cu_seqlens, hq, hkv, d, window, scale, plan, cache_key=None):
+        cache = plan.cache if cache_key is not None else None
+        hit = cache.take(cache_key) if cache is not None else None
+        if hit is not None:   # recompute of a checkpointed layer: reuse the first forward's result
+            out, lse = hit
+        else:
+            out = torch.empty(qkv.shape[0], hq * d, device=qkv.device, dtype=qkv.dtype)
+            lse = torch.empty(hq, qkv.shape[0], device=qkv.device, dtype=torch.float32)
+            ext().attn_fwd(qkv, sinks.float().contiguous(), plan.tiles, plan.cu, out, lse, hq,
+                           hkv, d, window, scale)
+            if cache is not None:
+                cache.offer(cache_key, out, lse)
         ctx.save_for_backward(qkv, sinks, out, lse)
         ctx.cfg = (hq, hkv, d, window, scale, plan)
         return out
@@ -97,7 +136,7 @@ class _AttentionKernel(torch.autograd.Function):
         dsinks = torch.zeros(hq, device=qkv.device, dtype=torch.float32)
         ext().attn_bwd(qkv, sinks.float().contiguous(), plan.kv_tiles, plan.cu, out,
                        dout.contiguous(), lse, dqkv, dsinks, hq, hkv, d, window, scale)
-        return dqkv, dsinks.to(sinks.dtype), None, None, None, None, None, None, None
+        return dqkv, dsinks.to(sinks.dtype), None, None, None, None, None, None, None, None
 
 
 class AttentionPlan:
@@ -125,6 +164,7 @@ class AttentionPlan:
         self.kv_tiles = torch.tensor(kv_order or [(0, 0, 0, 0)], dtype=torch.int32, device=device)
         self.cu = torch.tensor(cu, dtype=torch.int32, device=device)
         self.n_tiles = len(tiles)
+        self.cache: AttentionOutputCache | None = None   # set by a checkpointed training forward
 
 
 _HAS_KERNEL = None
@@ -142,10 +182,13 @@ def kernel_available() -> bool:
 
 def attention(qkv: torch.Tensor, sinks: torch.Tensor, cu_seqlens: torch.Tensor, hq: int,
               hkv: int, d: int, window: int = 0, scale: float | None = None,
-              plan: AttentionPlan | None = None) -> torch.Tensor:
+              plan: AttentionPlan | None = None, cache_key=None) -> torch.Tensor:
+    """``cache_key`` (e.g. the layer index) lets a checkpointed layer's recompute reuse the
+    output of its first forward when ``plan.cache`` is set (see AttentionOutputCache)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(d)
     if use_cuda_kernels(qkv) and kernel_available() and d == 64:
         if plan is None:
             plan = AttentionPlan(cu_seqlens, qkv.device)
-        return _AttentionKernel.apply(qkv, sinks, cu_seqlens, hq, hkv, d, window, scale, plan)
+        return _AttentionKernel.apply(qkv, sinks, cu_seqlens, hq, hkv, d, window, scale, plan,
+                                      cache_key)
     return _AttentionRef.apply(qkv, sinks, cu_seqlens, hq, hkv, d, window, scale)

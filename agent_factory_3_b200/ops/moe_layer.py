@@ -36,9 +36,12 @@ class ExpertWeights:
 
     _scratch: dict = {}
 
-    def __init__(self, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias):
+    def __init__(self, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, shards=None):
         self.gu_blocks, self.gu_scales, self.gu_bias = gu_blocks, gu_scales, gu_bias
         self.dn_blocks, self.dn_scales, self.dn_bias = dn_blocks, dn_scales, dn_bias
+        # parallel.fsdp.ExpertShards when the blocks / scales above are only this rank's
+        # experts; the full stack is then gathered (fused with the dequantisation) on use
+        self.shards = shards
 
     @classmethod
     def _buf(cls, key, shape, device):
@@ -49,19 +52,18 @@ class ExpertWeights:
             cls._scratch[k] = b
         return b
 
+    def _dequantized(self, which: str, blocks, scales) -> torch.Tensor:
+        E, N, Gk, _ = self.shards.shapes[which + "_blocks"] if self.shards else blocks.shape
+        out = self._buf(which, (E, N, Gk * 32), blocks.device) if blocks.is_cuda else None
+        if self.shards is not None:
+            return self.shards.dequantized(which, blocks, scales, out)
+        return mxfp4.dequantize(blocks, scales, out=out)
+
     def gate_up(self) -> torch.Tensor:
-        E, N, Gk, _ = self.gu_blocks.shape
-        if not self.gu_blocks.is_cuda:
-            return mxfp4.dequantize(self.gu_blocks, self.gu_scales)
-        out = self._buf("gu", (E, N, Gk * 32), self.gu_blocks.device)
-        return mxfp4.dequantize(self.gu_blocks, self.gu_scales, out=out)
+        return self._dequantized("gu", self.gu_blocks, self.gu_scales)
 
     def down(self) -> torch.Tensor:
-        E, N, Gk, _ = self.dn_blocks.shape
-        if not self.dn_blocks.is_cuda:
-            return mxfp4.dequantize(self.dn_blocks, self.dn_scales)
-        out = self._buf("dn", (E, N, Gk * 32), self.dn_blocks.device)
-        return mxfp4.dequantize(self.dn_blocks, self.dn_scales, out=out)
+        return self._dequantized("dn", self.dn_blocks, self.dn_scales)
 
     @classmethod
     def release_scratch(cls):
@@ -182,7 +184,8 @@ class MoEFn(torch.autograd.Function):
 def _mxfp4_direct(xn: torch.Tensor, experts: ExpertWeights, E: int, top_k: int) -> bool:
     """Inference with few rows per expert and f16-exact scales: run the experts on the MXFP4
     bytes directly.  AF3_MOE_MXFP4=0/1 forces the choice (the scale check still applies)."""
-    if not xn.is_cuda or not use_cuda_kernels(xn) or not experts.f16_exact():
+    if (not xn.is_cuda or not use_cuda_kernels(xn) or experts.shards is not None
+            or not experts.f16_exact()):
         return False
     flag = os.environ.get("AF3_MOE_MXFP4")
     if flag is not None:

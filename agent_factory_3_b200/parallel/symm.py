@@ -20,6 +20,44 @@ from ..ops._ext import ext
 FLAG_BYTES = 256
 
 
+class PeerMappedBuffer:
+    """``nbytes`` of device memory on this rank, mapped by every other rank of ``group``.
+
+    ``local`` is this rank's buffer (uint8 tensor); ``bases[j]`` is rank j's buffer as a
+    device address valid on this rank (its own for j == rank).  Used for data that never
+    changes after set-up (sharded frozen weights), so readers need no synchronisation beyond
+    the collective that exchanged the handles."""
+
+    def __init__(self, nbytes: int, group=None, device: torch.device | None = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("peer mapping supports at most 8 ranks (one NVLink domain)")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.local, handle = ext().symm_alloc(int(nbytes), self.device.index)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened: list[int] = []
+        self.bases: list[int] = []
+        with torch.cuda.device(self.device):
+            for j, h in enumerate(handles):
+                if j == self.rank:
+                    self.bases.append(self.local.data_ptr())
+                else:
+                    p = ext().ipc_open(h)
+                    self._opened.append(p)
+                    self.bases.append(p)
+
+    def close(self) -> None:
+        for p in self._opened:
+            try:
+                ext().ipc_close(p)
+            except Exception:  # noqa: BLE001 - unmapping at exit is best effort
+                pass
+        self._opened.clear()
+
+
 class SymmetricWorkspace:
     def __init__(self, set_bytes: int, group=None, device: torch.device | None = None,
                  sets: int = 2):

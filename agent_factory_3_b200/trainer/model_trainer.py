@@ -7,9 +7,10 @@ methods (``train_step``, ``reset_optimizer_state``, ``save_model``, ``load_model
 PEFT-format adapters.
 
 What differs (B200 design):
-  * one process per GPU; the frozen MXFP4 base is resident on every GPU (180 GB HBM holds
-    gpt-oss-120b's 65 GB of weights plus 131k-token activations), so there is no per-layer
-    all-gather on the critical path; only trainable state is reduced across ranks;
+  * one process per GPU; the frozen MXFP4 experts are either resident on every GPU (180 GB HBM
+    holds gpt-oss-120b's 65 GB of weights plus 131k-token activations) or, with
+    ``shard_base_weights``, split over the ranks and gathered over NVLink inside the kernel
+    that dequantises a layer's experts (parallel/fsdp.py); only trainable state is reduced;
   * gradients of all trainable tensors live in one flat fp32 buffer so the data-parallel
     reduction is a single NCCL all-reduce (or reduce-scatter when the optimizer state is
     sharded) instead of per-parameter collectives;
@@ -65,6 +66,7 @@ def build_model(config: TrainingConfig, device, model_config: GptOssConfig | Non
     else:
         model.init_random(seed=config.random_init_seed or 0)
     model.gradient_checkpointing = config.gradient_checkpointing
+    model.attention_cache_bytes = int(config.attention_cache_gb * 1e9)
     if config.training_mode == "full":
         for n, p in model.named_parameters():
             train = config.trainable_modules is None or any(m in n for m in config.trainable_modules)
@@ -87,6 +89,12 @@ class ModelTrainer(RPCMixin):
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
         self.model = model if model is not None else build_model(config, self.device, model_config)
+        self.expert_shards = None
+        if config.shard_base_weights and self.distributed and self.world_size > 1:
+            # FSDP-style: each rank keeps 1/W of every layer's frozen MXFP4 experts; a layer's
+            # full stack is gathered over NVLink inside its dequantisation kernel
+            from ..parallel.fsdp import shard_expert_weights
+            self.expert_shards = shard_expert_weights(self.model)
         self.trainable = [p for p in self.model.parameters() if p.requires_grad]
         if not self.trainable:
             raise RuntimeError("no trainable parameters (check lora_target_modules / trainable_modules)")
@@ -105,6 +113,7 @@ class ModelTrainer(RPCMixin):
         self.step_count = 0
         self.last_step_events = None
         self._outbox = None
+        self.last_step_h2d_bytes = self.last_step_d2h_bytes = self.last_step_tokens = 0
         RPCMixin.__init__(self, group=rpc_group)
 
     # ------------------------------------------------------------------ setup
@@ -223,6 +232,7 @@ class ModelTrainer(RPCMixin):
                              grad_norm.float() if grad_norm is not None else torch.zeros((), device=self.device)])
         red = all_reduce_metric_states(states, extra=extra)
         vals = red.tolist()  # the step's single device->host read
+        self.last_step_d2h_bytes = 4 * (len(vals) + len(states))
         metrics = {"loss": vals[0], "learning_rate": float(self.optimizer.param_groups[0]["lr"])}
         if grad_norm is not None:
             metrics["grad_norm"] = vals[1] / self.world_size  # every rank holds the global norm
@@ -285,8 +295,13 @@ class ModelTrainer(RPCMixin):
         self.model.train()
         loss_sum = torch.zeros((), device=self.device)
         states: dict[str, MeanMetricState] = {}
+        self.last_step_h2d_bytes = 0
+        self.last_step_tokens = 0
         for idx in plan:
             host = self.collator([samples[i] for i in idx])
+            self.last_step_h2d_bytes += sum(v.numel() * v.element_size() for k, v in host.items()
+                                            if isinstance(v, torch.Tensor) and k != "cu_seqlens")
+            self.last_step_tokens += int(host["num_tokens"])
             batch = self._to_device(host)
             loss, st = self._microbatch(batch)
             loss.backward()

@@ -16,6 +16,9 @@ class TrainingConfig(BaseModel):
     model_id: str = "gpt-oss-120b"          # preset name or HF-format checkpoint directory
     attn_implementation: str = "sm100"       # kept for config compatibility; one kernel path
     gradient_checkpointing: bool = True
+    # GB of full-attention layer outputs (O + LSE) kept from the forward so the checkpoint
+    # recompute skips those attention kernels; 0 recomputes everything
+    attention_cache_gb: float = 0.0
     use_reentrant: bool = False
     model_use_cache: bool = False
     model_init_kwargs: dict | None = None
@@ -91,7 +94,9 @@ class TrainingConfig(BaseModel):
     wandb_notes: str = ""
     wandb_resume: bool = True
     # parallelism (B200 engine)
-    shard_base_weights: bool = False          # True: FSDP-style per-layer all-gather of frozen base
+    # FSDP-style sharding of the frozen MXFP4 experts over the data-parallel ranks; a layer's
+    # experts are gathered over NVLink inside their dequantisation kernel (parallel/fsdp.py)
+    shard_base_weights: bool = False
 
     @computed_field
     @property

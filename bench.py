@@ -1,25 +1,42 @@
 #!/usr/bin/env python
-"""Headline benchmark: gpt-oss-120b MXFP4 LoRA RL training step on B200s.
+"""Headline benchmark: gpt-oss-120b MXFP4 LoRA RL training step, plus the rollout-decode rate
+of the same model, on one node of B200s.
 
-Config: gpt-oss-120b architecture with random-init weights (experts
-quantized to MXFP4), LoRA r=32 / alpha=64 on attention and experts, per GPU one packed
-microbatch of 131072 tokens made of samples with lengths uniform in [4096, 131072], R3 replay of
-recorded (synthetic) top-4 expert ids, activation checkpointing, fused linear-logprob/entropy
-over the 201088 vocabulary, DDIS loss against synthetic rollout log-probs, AdamW step.
-Weak scaling: every rank trains its own 131072 tokens; gradients are all-reduced over NCCL.
+Training: gpt-oss-120b architecture with random-init weights (experts
+quantized to MXFP4), LoRA r=32 / alpha=64 on attention and experts, 131072 packed tokens per
+GPU made of samples with lengths uniform in [4096, 131072], R3 replay of recorded (synthetic)
+top-4 expert ids, activation checkpointing, fused linear-logprob/entropy over the 201088
+vocabulary, DDIS loss against synthetic rollout log-probs, AdamW step with the optimizer state
+sharded over the ranks.  Every step goes through the public API ``ModelTrainer.train_step``:
+rank 0 holds the step's whole sample pool, the trainer's packing plan assigns buckets to ranks
+and scatters each rank its own samples, each rank collates, copies its pinned batch to the
+device, trains, and the step's metrics come back to the host.  Weak scaling: the pool holds
+131072 tokens per GPU and every rank's share has the same length profile (its own random
+tokens and routing), so per-GPU work is fixed as N grows.
+
+Decode (config 4, a steady-state window): 128 concurrent trajectories, each a 2048-token
+random prompt generating 8192 tokens with a 256-token random tool response appended every 1024
+generated tokens, bf16 paged KV, temperature 1.0, tensor parallel over the N GPUs.  The window
+places trajectory i at generated position 64*i (spread evenly over the 8192), prefills its
+context (prompt + generated tokens so far + the tool responses so far) untimed, then times
+every trajectory generating the next ``--decode-tokens`` tokens, tool responses included (a
+trajectory that reaches a multiple of 1024 continues as a new request on the prefix-cached
+context plus 256 tool tokens).  The window's mean context and tool-response rate are those of
+the full 8192-token run.  Then the same window with the 1-layer block-draft model proposing
+8-token blocks.
 
     python bench.py --gpus N --steps K --warmup W            (N>1 under torch.distributed.run)
     python bench.py --impl reference ...                     (the reference's own stack)
 
-Prints one JSON line on rank 0.  ``value`` is the device-timed throughput (CUDA events around
-K steps, max over ranks); ``e2e`` is the same K steps measured by the host clock through the
-public API (``ModelTrainer.train_packed_batch``) including the host->device copy of each step's
-pinned inputs and the device->host read of each step's loss.
+Prints one JSON line on rank 0.  ``value`` is the device-timed training throughput (CUDA events
+on every rank around the K steps, max over ranks); ``e2e`` is the same K steps on the host
+clock of the driving process; ``decode`` holds the decode-window numbers.
 """
 from __future__ import annotations
 
 import argparse
 import datetime
+import gc
 import json
 import os
 import statistics
@@ -45,40 +62,46 @@ def parse_args():
     ap.add_argument("--lora-alpha", type=int, default=64)
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--shard-optimizer", action="store_true",
-                    help="shard the LoRA optimizer state over the ranks (reduce-scatter + "
-                         "all-gather) instead of one all-reduce")
+    ap.add_argument("--replicate-optimizer", action="store_true",
+                    help="keep the whole AdamW state on every rank (one all-reduce) instead of "
+                         "the default sharded optimizer state")
+    ap.add_argument("--attention-cache-gb", type=float, default=12.0,
+                    help="GB of full-attention outputs kept for the checkpoint recompute")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode window")
+    ap.add_argument("--decode-requests", type=int, default=128)
+    ap.add_argument("--decode-tokens", type=int, default=256,
+                    help="tokens each trajectory generates in the timed decode window")
+    ap.add_argument("--no-spec", action="store_true", help="skip the block-draft decode window")
     ap.add_argument("--trace", default=None,
                     help="after the timed steps, run one more step under torch.profiler and write "
                          "its per-kernel device-time table (text) to this path")
     return ap.parse_args()
 
 
-def write_trace(step, path: str) -> None:
-    """One untimed step under torch.profiler: kernel table sorted by device time."""
-    import torch
-    from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
-        step()
-        torch.cuda.synchronize()
-    table = prof.key_averages().table(sort_by="self_device_time_total", row_limit=60,
-                                      max_name_column_width=90)
-    with open(path, "w") as f:
-        f.write(table)
-
-
 def reference_unavailable(args) -> None:
-    reason = ("reference training path cannot run offline: it imports triton_kernels "
-              "(matmul_ogs, routing) and accelerate/peft, which are not installed and not in "
-              "the wheelhouse (pip --no-deps install into baseline/_ref succeeds, import fails)")
-    try:
-        sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref"))
-        import agent_factory_3.models.gpt_oss.quantization  # noqa: F401
-        import agent_factory_3.trainer.model_trainer  # noqa: F401
-        reason = "reference imports but its FSDP2/accelerate launch path is not wired in this bench"
-    except Exception as e:  # noqa: BLE001
-        reason += f" ({type(e).__name__}: {e})"
-    print(json.dumps({"impl": "reference", "unavailable": reason}))
+    """The reference's own training entry point, run unmodified from baseline/_ref if it
+    imports; otherwise the exact import error, one line."""
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "agent_factory_3")):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference not installed in baseline/_ref (pip install --target failed)"}))
+        return
+    sys.path.insert(0, ref)
+    missing = []
+    for mod in ("agent_factory_3.models.gpt_oss.quantization",
+                "agent_factory_3.trainer.model_trainer"):
+        try:
+            __import__(mod)
+        except Exception as e:  # noqa: BLE001 - report exactly what failed
+            missing.append(f"{mod}: {type(e).__name__}: {e}")
+    if missing:
+        reason = ("the reference's training path does not import offline (its dependencies "
+                  "triton_kernels / accelerate / peft are not installed and not in the "
+                  "wheelhouse): " + "; ".join(missing))
+    else:
+        reason = ("the reference's modules import, but its launch path needs accelerate's FSDP2 "
+                  "launcher and an sglang server, neither of which is available offline")
+    print(json.dumps({"impl": "reference", "unavailable": reason[:1500]}))
 
 
 class ClockSampler:
@@ -119,9 +142,7 @@ class ClockSampler:
                 self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
-        sm = []
-        maxes = []
-        reasons = set()
+        sm, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for s in self.samples:
             try:
@@ -137,45 +158,317 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_samples(args, rank: int, n_layers: int, n_experts: int, top_k: int, vocab: int, device):
-    """Synthetic agentic traces of one rank: random ids, a prompt prefix, rollout log-probs,
-    group-normalised Bernoulli advantages and recorded top-k expert ids per layer."""
+def length_profile(args) -> list[int]:
+    """Sample lengths of one GPU's share: uniform in [min_len, max_len] until the share holds
+    ``--tokens`` tokens (the last sample is cut to fit)."""
+    import numpy as np
+    rng = np.random.default_rng(args.seed)
+    lens, left = [], args.tokens
+    while left > 0:
+        n = min(int(rng.integers(args.min_len, args.max_len + 1)), left)
+        lens.append(n)
+        left -= n
+    return lens
+
+
+def make_pool(args, world: int, n_layers: int, n_experts: int, top_k: int, vocab: int, device):
+    """The step's sample pool: ``world`` shares of the same length profile, each with its own
+    random ids, prompt prefix, rollout log-probs, group-normalised Bernoulli advantages and
+    recorded top-k expert ids per layer."""
     import numpy as np
     import torch
 
     from agent_factory_3_b200.trainer.types import TrainingSample
 
-    rng = np.random.default_rng(args.seed * 1000 + rank)
-    lens = []
-    left = args.tokens
-    while left > 0:
-        n = int(rng.integers(args.min_len, args.max_len + 1))
-        n = min(n, left)
-        lens.append(n)
-        left -= n
-    rewards = rng.integers(0, 2, size=len(lens)).astype(np.float32)
-    adv = rewards - rewards.mean()
-    if adv.std() > 0:
-        adv = adv / (adv.std() + 1e-6)
+    lens = length_profile(args)
+    pool = []
+    for share in range(world):
+        rng = np.random.default_rng(args.seed * 1000 + share + 1)
+        rewards = rng.integers(0, 2, size=len(lens)).astype(np.float32)
+        adv = rewards - rewards.mean()
+        adv = adv / (adv.std() + 1e-6) if adv.std() > 0 else \
+            np.where(np.arange(len(lens)) % 2 == 0, 1.0, -1.0).astype(np.float32)
+        g = torch.Generator(device=device).manual_seed(args.seed * 1000 + share + 1)
+        for i, n in enumerate(lens):
+            prompt = min(2048, n // 4)
+            comp = np.zeros(n, np.int32)
+            comp[prompt:] = 1
+            ids = rng.integers(0, vocab, n).astype(np.int64)
+            gen = np.where(comp > 0, -np.log(vocab) + rng.normal(0, 0.05, n), 0).astype(np.float32)
+            routing = np.empty((n, n_layers, top_k), np.uint8)
+            for c0 in range(0, n, 16384):           # distinct random experts per (token, layer)
+                c1 = min(n, c0 + 16384)
+                r = torch.rand((c1 - c0) * n_layers, n_experts, generator=g, device=device)
+                routing[c0:c1] = r.topk(top_k, dim=-1).indices.to(torch.uint8).reshape(
+                    c1 - c0, n_layers, top_k).cpu().numpy()
+                del r
+            pool.append(TrainingSample(
+                sample_id=f"s{share}_{i}", input_ids=ids, completion_mask=comp,
+                gen_logprobs=gen, advantages=(comp * adv[i]).astype(np.float32),
+                routing_indices=routing, seq_token_count=int(comp.sum()),
+                prompt_sequence_count=8, prompt_id=f"g{share}_{i // 8}", divisor=8.0))
+    torch.cuda.empty_cache()
+    return pool, lens
+
+
+def bench_trainer_class():
+    """ModelTrainer plus three control-plane calls that every rank runs in step with rank 0
+    (they ride the trainer's own RPC): a device barrier, a CUDA event mark and the per-rank
+    statistics of the timed region."""
+    import torch
+    import torch.distributed as dist
+
+    from agent_factory_3_b200.ops import _ext
+    from agent_factory_3_b200.parallel.rpc import rpc_method
+    from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
+
+    class BenchTrainer(ModelTrainer):
+        @rpc_method(gather=False)
+        def bench_sync(self):
+            torch.cuda.synchronize()
+            if self.distributed and self.world_size > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+
+        @rpc_method(gather=False)
+        def bench_mark(self, tag: str):
+            if not hasattr(self, "_marks"):
+                self._marks = {}
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks[tag] = (ev, _ext.launch_count(), time.perf_counter())
+            self._io = getattr(self, "_io", [0, 0, 0])
+            if tag == "t0":
+                self._io = [0, 0, 0]
+
+        @rpc_method(gather=False)
+        def bench_accumulate_io(self):
+            self._io[0] += self.last_step_h2d_bytes
+            self._io[1] += self.last_step_d2h_bytes
+            self._io[2] += self.last_step_tokens
+
+        @rpc_method(gather=True, reduce="concat")
+        def bench_stats(self, a: str, b: str, steps: int):
+            torch.cuda.synchronize()
+            (e0, l0, _), (e1, l1, _) = self._marks[a], self._marks[b]
+            return [{"rank": self.rank, "ms": e0.elapsed_time(e1) / steps,
+                     "launches": l1 - l0, "h2d": self._io[0] / steps, "d2h": self._io[1] / steps,
+                     "tokens": self._io[2] / steps,
+                     "max_mem_gb": torch.cuda.max_memory_allocated() / 1e9}]
+
+    return BenchTrainer
+
+
+def run_train(args, world: int, rank: int, device):
+    import torch
+
+    from agent_factory_3_b200.models.gpt_oss import GptOssConfig
+    from agent_factory_3_b200.trainer.training_config import TrainingConfig
+
+    mcfg = GptOssConfig.preset(args.model)
+    if args.layers:
+        mcfg.num_hidden_layers = args.layers
+        mcfg.layer_types = mcfg.layer_types[: args.layers]
+    tcfg = TrainingConfig(
+        model_id=args.model, lora_r=args.lora_r, lora_alpha=args.lora_alpha,
+        lora_target_modules=["q_proj", "k_proj", "v_proj", "o_proj", "gate_up_proj", "down_proj"],
+        max_capacity=args.tokens, pad_to_multiple_of_training=1024, random_init_seed=0,
+        use_routing_replay=True, gradient_checkpointing=True, lr_warmup_steps=0,
+        learning_rate=1e-5, shard_optimizer_state=not args.replicate_optimizer,
+        attention_cache_gb=args.attention_cache_gb)
+    BenchTrainer = bench_trainer_class()
+    t_init = time.perf_counter()
+    trainer = BenchTrainer(tcfg, model_config=mcfg, device=device)
+    torch.cuda.synchronize()
+    t_init = time.perf_counter() - t_init
+    if rank != 0:
+        trainer.rpc_worker_loop()      # rank 0 drives every step; this rank follows
+        out = None
     else:
-        adv = np.where(np.arange(len(lens)) % 2 == 0, 1.0, -1.0).astype(np.float32)
-    g = torch.Generator(device=device).manual_seed(args.seed * 1000 + rank)
-    samples = []
-    for i, n in enumerate(lens):
-        prompt = min(2048, n // 4)
-        comp = np.zeros(n, np.int32)
-        comp[prompt:] = 1
-        ids = rng.integers(0, vocab, n).astype(np.int64)
-        gen = np.where(comp > 0, -np.log(vocab) + rng.normal(0, 0.05, n), 0).astype(np.float32)
-        # distinct random experts per (token, layer)
-        r = torch.rand(n * n_layers, n_experts, generator=g, device=device)
-        routing = r.topk(top_k, dim=-1).indices.to(torch.uint8).reshape(n, n_layers, top_k).cpu().numpy()
-        samples.append(TrainingSample(
-            sample_id=f"r{rank}s{i}", input_ids=ids, completion_mask=comp, gen_logprobs=gen,
-            advantages=(comp * adv[i]).astype(np.float32), routing_indices=routing,
-            seq_token_count=int(comp.sum()), prompt_sequence_count=8, prompt_id=f"g{i // 8}",
-            divisor=8.0))
-    return samples, lens
+        pool, lens = make_pool(args, world, mcfg.num_hidden_layers, mcfg.num_local_experts,
+                               mcfg.num_experts_per_tok, mcfg.vocab_size, device)
+        for _ in range(args.warmup):
+            trainer.train_step(pool)
+        trainer.bench_sync()
+        clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(device).uuid))
+        clocks.start()
+        trainer.bench_mark("t0")
+        t0 = time.perf_counter()
+        losses = []
+        for _ in range(args.steps):
+            metrics = trainer.train_step(pool)    # ends with the step's device->host read
+            trainer.bench_accumulate_io()
+            losses.append(metrics["loss"])
+        wall = time.perf_counter() - t0
+        trainer.bench_mark("t1")
+        trainer.bench_sync()
+        clk = clocks.stop()
+        stats = trainer.bench_stats("t0", "t1", args.steps)
+        if args.trace:
+            from torch.profiler import ProfilerActivity, profile
+            with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+                trainer.train_step(pool)
+                torch.cuda.synchronize()
+            with open(args.trace, "w") as f:
+                f.write(prof.key_averages().table(sort_by="self_device_time_total", row_limit=60,
+                                                  max_name_column_width=90))
+        trainer.rpc_shutdown()
+        dev_ms = max(s["ms"] for s in stats)
+        tokens = sum(s["tokens"] for s in stats)
+        out = {"dev_ms": dev_ms, "wall_ms": wall * 1000.0 / args.steps, "tokens": tokens,
+               "clocks": clk, "stats": stats, "losses": losses, "lens": lens,
+               "n_samples": len(pool), "init_s": t_init, "layers": mcfg.num_hidden_layers,
+               "packing": trainer._packing_stats.__dict__}
+    del trainer
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decode(args, world: int, rank: int, device, spec: bool):
+    """One timed decode window (see the module docstring).  Rank 0 drives the engine; under
+    N>1 the other ranks follow its steps (tensor parallel)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from agent_factory_3_b200.engine.scheduler import Engine, Request
+    from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM
+    from agent_factory_3_b200.ops import _ext
+
+    cfg = GptOssConfig.preset(args.model)
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
+        cfg.layer_types = cfg.layer_types[: args.layers]
+    R, gen_total, prompt, tool, every = args.decode_requests, 8192, 2048, 256, 1024
+    win = args.decode_tokens
+    starts = [(i * gen_total) // R for i in range(R)]
+    ctx = [prompt + g + tool * (g // every) for g in starts]
+    page = 64
+    t_init = time.perf_counter()
+    model = GptOssForCausalLM(cfg, device=device).init_random(args.seed).eval()
+    tp = shards = None
+    if world > 1:
+        from agent_factory_3_b200.engine.tp import TPContext, broadcast_model, shard_model
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+        broadcast_model(model)
+        shards = shard_model(model, rank, world, free_full=True)
+        torch.cuda.empty_cache()
+        tp = TPContext(None, cpu_group, device, max_tokens=16384 + R * 9, hidden=cfg.hidden_size)
+    drafter = None
+    if spec:
+        from agent_factory_3_b200.engine.spec import BlockDraftModel
+        drafter = BlockDraftModel.from_target(model, n_layers=1, block=8, seed=args.seed + 1)
+    need_tokens = sum(c + win + tool * 2 + 16 for c in ctx)
+    eng = Engine(model, num_pages=need_tokens // page + 4 * R + 64, page_size=page,
+                 max_running=R, max_prefill_tokens=16384, tp=tp, tp_shards=shards,
+                 drafter=drafter, max_context_tokens=prompt + gen_total + tool * 8 + 64)
+    torch.cuda.synchronize()
+    t_init = time.perf_counter() - t_init
+    if rank != 0:
+        eng.runner.follow()
+        tp.shutdown()
+        del eng, model
+        gc.collect()
+        torch.cuda.empty_cache()
+        return None
+    eng.start()
+    rng = np.random.default_rng(args.seed + 7)
+    lock = threading.Lock()
+    done = threading.Event()
+    state = {"left": R, "gen": 0, "requests": 0, "tool_tokens": 0}
+
+    def run_batch(reqs, timeout):
+        ev = threading.Event()
+        n = {"left": len(reqs)}
+
+        def cb(out):
+            if out["finished"]:
+                with lock:
+                    n["left"] -= 1
+                    if n["left"] == 0:
+                        ev.set()
+        for r in reqs:
+            r.on_output = cb
+            eng.submit(r)
+        if not ev.wait(timeout):
+            raise TimeoutError("decode prefill did not finish")
+
+    # untimed: prefill every trajectory's context (registers its pages in the prefix cache)
+    t_pre = time.perf_counter()
+    contexts = [rng.integers(0, cfg.vocab_size, c).tolist() for c in ctx]
+    pre = [Request(input_ids=c, max_new_tokens=1, temperature=1.0, seed=i, stop_token_ids=[])
+           for i, c in enumerate(contexts)]
+    run_batch(pre, 3600)
+    for c, r in zip(contexts, pre):
+        c.extend(r.output_ids)
+    t_pre = time.perf_counter() - t_pre
+
+    def continue_traj(i, made):
+        """Submit trajectory i's next request: up to its next 1024 boundary, at most the
+        window's remaining tokens."""
+        pos = starts[i] + made
+        n = min(win - made, every - pos % every)
+        r = Request(input_ids=list(contexts[i]), max_new_tokens=n, temperature=1.0,
+                    seed=1000 + i * 97 + made, stop_token_ids=[])
+
+        def cb(out, r=r, i=i, made=made):
+            if not out["finished"]:
+                return
+            got = len(r.output_ids)
+            with lock:
+                state["gen"] += got
+            contexts[i].extend(r.output_ids)
+            total = made + got
+            if total >= win or r.finish_reason.get("type") == "abort":
+                with lock:
+                    state["left"] -= 1
+                    if state["left"] == 0:
+                        done.set()
+                return
+            if (starts[i] + total) % every == 0:      # tool call returns 256 tokens
+                contexts[i].extend(rng.integers(0, cfg.vocab_size, tool).tolist())
+                with lock:
+                    state["tool_tokens"] += tool
+            continue_traj(i, total)
+        r.on_output = cb
+        with lock:
+            state["requests"] += 1
+        eng.submit(r)
+
+    torch.cuda.synchronize()
+    l0 = _ext.launch_count()
+    t0 = time.perf_counter()
+    for i in range(R):
+        continue_traj(i, 0)
+    ok = done.wait(1800)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    launches = _ext.launch_count() - l0
+    eng.stop()
+    err = None
+    try:
+        _ext.check_device_error()
+    except Exception as e:  # noqa: BLE001
+        err = str(e)[:200]
+    res = {"tok_per_s": round(state["gen"] / wall, 1) if ok else None, "completed": ok,
+           "generated_tokens": state["gen"], "window_s": round(wall, 2),
+           "requests": state["requests"], "tool_tokens_prefilled": state["tool_tokens"],
+           "prefill_setup_s": round(t_pre, 1), "init_s": round(t_init, 1),
+           "mean_context": round(float(np.mean(ctx)) + win / 2, 1), "launches_rank0": launches}
+    if drafter is not None:
+        res["spec"] = {"draft": "1-layer random-init block draft", "block": 8,
+                       "accept_length": round(eng.spec_accept_length, 3),
+                       "accept_rate": round(eng.spec_accept_rate, 4),
+                       "verifies": eng.spec_verifies}
+    if err:
+        res["device_error"] = err
+    if tp is not None:
+        tp.shutdown()
+    del eng, model
+    gc.collect()
+    torch.cuda.empty_cache()
+    return res
 
 
 def main():
@@ -193,77 +486,24 @@ def main():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
 
-    from agent_factory_3_b200.models.gpt_oss import GptOssConfig
-    from agent_factory_3_b200.ops import _ext
-    from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
-    from agent_factory_3_b200.trainer.training_config import TrainingConfig
-
-    mcfg = GptOssConfig.preset(args.model)
-    if args.layers:
-        mcfg = GptOssConfig.preset(args.model)
-        mcfg.num_hidden_layers = args.layers
-        mcfg.layer_types = mcfg.layer_types[: args.layers]
-    tcfg = TrainingConfig(
-        model_id=args.model, lora_r=args.lora_r, lora_alpha=args.lora_alpha,
-        lora_target_modules=["q_proj", "k_proj", "v_proj", "o_proj", "gate_up_proj", "down_proj"],
-        max_capacity=args.tokens, pad_to_multiple_of_training=1024, random_init_seed=0,
-        use_routing_replay=True, gradient_checkpointing=True, lr_warmup_steps=0,
-        learning_rate=1e-5, shard_optimizer_state=args.shard_optimizer)
-    t_init = time.perf_counter()
-    trainer = ModelTrainer(tcfg, model_config=mcfg, device=device)
-    torch.cuda.synchronize()
-    t_init = time.perf_counter() - t_init
-    samples, lens = make_samples(args, rank, mcfg.num_hidden_layers, mcfg.num_local_experts,
-                                 mcfg.num_experts_per_tok, mcfg.vocab_size, device)
-    host_batch = trainer.collator(samples)
-    tokens_per_rank = int(host_batch["num_tokens"])
-    h2d_bytes = sum(v.numel() * v.element_size() for k, v in host_batch.items()
-                    if isinstance(v, torch.Tensor) and k != "cu_seqlens")
-
-    def step():
-        loss = trainer.train_packed_batch(host_batch)
-        return loss.item()  # device->host read of the step's result
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
-    clocks = ClockSampler(uuid)
-    clocks.start()
-    launches0 = _ext.launch_count()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    ev0.record()
-    losses = []
-    for _ in range(args.steps):
-        losses.append(step())
-    ev1.record()
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    launches = _ext.launch_count() - launches0
-    dev_ms = ev0.elapsed_time(ev1) / args.steps
-    wall_ms = wall * 1000.0 / args.steps
-    stats = torch.tensor([dev_ms, wall_ms], device=device, dtype=torch.float64)
-    tok = torch.tensor([float(tokens_per_rank)], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-        dist.all_reduce(tok, op=dist.ReduceOp.SUM)
-    dev_ms, wall_ms = stats.tolist()
-    total_tokens = tok.item()
-    value = total_tokens / (dev_ms / 1000.0)
-    e2e = total_tokens / (wall_ms / 1000.0)
+    tr = run_train(args, world, rank, device)
+    decode = None
+    if not args.no_decode:
+        decode = {}
+        for spec in ((False,) if args.no_spec else (False, True)):
+            try:
+                r = run_decode(args, world, rank, device, spec)
+            except Exception as e:  # noqa: BLE001 - the training number still stands
+                r = {"error": f"{type(e).__name__}: {e}"[:300]}
+            if rank == 0:
+                decode["block_draft" if spec else "plain"] = r
     if rank == 0:
+        total_tokens = tr["tokens"]
+        value = total_tokens / (tr["dev_ms"] / 1000.0)
+        e2e = total_tokens / (tr["wall_ms"] / 1000.0)
+        st = tr["stats"]
         out = {
             "metric": METRIC,
             "value": round(value, 1),
@@ -271,7 +511,7 @@ def main():
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(dev_ms, 2),
+            "ms_per_step": round(tr["dev_ms"], 2),
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
@@ -279,25 +519,37 @@ def main():
             "data": "synthetic (random token ids, random-init weights, MXFP4 experts)",
             "impl": "ours",
             "config": {"model": args.model, "global_batch": int(total_tokens),
-                       "tokens_per_gpu": tokens_per_rank, "seq_len": args.max_len,
-                       "sample_lengths": f"uniform[{args.min_len},{args.max_len}] packed",
-                       "samples_per_gpu": len(lens), "lora": f"r{args.lora_r}/a{args.lora_alpha} attn+experts",
+                       "tokens_per_gpu": args.tokens, "seq_len": args.max_len,
+                       "sample_lengths": f"uniform[{args.min_len},{args.max_len}] packed, same "
+                                         f"length profile on every GPU: {tr['lens']}",
+                       "samples_per_step": tr["n_samples"],
+                       "lora": f"r{args.lora_r}/a{args.lora_alpha} attn+experts",
                        "routing_replay": True, "activation_checkpointing": True,
+                       "attention_cache_gb": args.attention_cache_gb,
+                       "optimizer": "replicated" if args.replicate_optimizer else "sharded",
                        "parallelism": f"dp{world}" if world > 1 else "single",
-                       "layers": mcfg.num_hidden_layers,
+                       "layers": tr["layers"],
                        "l2": "inputs larger than L2 (65 GB of weights stream every step)"},
-            "clocks": clk,
+            "clocks": tr["clocks"],
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s (train, whole job)",
-                    "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": 4,
-                    "api": "ModelTrainer.train_packed_batch"},
-            "gpu_launches": int(launches),
-            "init_s": round(t_init, 1),
-            "max_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1),
-            "loss": losses[-1],
+                    "h2d_bytes_per_step": int(sum(s["h2d"] for s in st)),
+                    "d2h_bytes_per_step": int(sum(s["d2h"] for s in st)),
+                    "api": "ModelTrainer.train_step (sample scatter, collation, pinned H2D copy, "
+                           "step, metrics D2H)"},
+            "gpu_launches": int(sum(s["launches"] for s in st)),
+            "per_rank_ms": [round(s["ms"], 1) for s in st],
+            "init_s": round(tr["init_s"], 1),
+            "max_mem_gb": round(max(s["max_mem_gb"] for s in st), 1),
+            "loss": tr["losses"][-1],
         }
+        if decode is not None:
+            d = {"metric": "rollout decode tok/s (config 4 steady-state window, whole job)",
+                 "tp": world, "requests": args.decode_requests,
+                 "window_tokens_per_trajectory": args.decode_tokens,
+                 "timing": "host clock around the window; engine idle and device synchronised "
+                           "at both ends", **decode}
+            out["decode"] = d
         print(json.dumps(out), flush=True)
-    if args.trace:
-        write_trace(step, args.trace if world == 1 else f"{args.trace}.rank{rank}")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -11,6 +11,7 @@ pytestmark = pytest.mark.gpu
 
 CASES = [
     ([300], 0), ([300, 129, 75, 1], 0), ([300, 129, 75, 1], 32), ([517], 128), ([64, 700], 128),
+    ([2048, 300], 0),   # many unmasked blocks: the FMA-pipe exponentials and lazy rescaling
 ]
 
 

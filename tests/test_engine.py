@@ -174,3 +174,42 @@ def test_lora_hot_swap_and_merged_reload(tmp_path):
     assert_greedy(tr.model, prompt, merged["output_ids"])   # LoRA folded into the base weights
     assert merged["meta_info"]["weight_version"] == "m1"
     assert bad == 400
+
+
+def test_top_logprobs_are_the_k_best_tokens():
+    """``top_logprobs_num`` returns, per generated token, the k most likely tokens with their
+    log-probabilities under the request's temperature, best first; under greedy decoding the
+    first alternative is the generated token itself."""
+    import threading
+
+    from agent_factory_3_b200.engine.scheduler import Request
+    model = tiny_model()
+    eng = Engine(model, num_pages=64, page_size=16).start()
+    try:
+        prompt = list(range(5, 25))
+        done = threading.Event()
+        box = {}
+        r = Request(input_ids=prompt, max_new_tokens=4, temperature=0.0, return_logprob=True,
+                    top_logprobs_num=5)
+        r.on_output = lambda out: (box.update(out), done.set()) if out["finished"] else None
+        eng.submit(r)
+        assert done.wait(120)
+    finally:
+        eng.stop()
+    meta = box["meta_info"]
+    out = box["output_ids"]
+    tops = meta["output_top_logprobs"]
+    assert len(tops) == len(out) == 4
+    ids = prompt + out[:-1]
+    with torch.no_grad():
+        h = model.forward_hidden(torch.tensor(ids), torch.arange(len(ids)),
+                                 torch.tensor([0, len(ids)], dtype=torch.int32))
+        lp = torch.log_softmax(model.logits(h[len(prompt) - 1:]).float(), -1)
+    for pos, row in enumerate(tops):
+        assert len(row) == 5 and all(len(e) == 3 for e in row)
+        vals = [e[0] for e in row]
+        assert vals == sorted(vals, reverse=True)
+        assert row[0][1] == out[pos]
+        want_v, want_i = lp[pos].topk(5)
+        assert [e[1] for e in row][:2] == want_i.tolist()[:2] or abs(vals[0] - vals[1]) < 1e-4
+        assert abs(vals[0] - float(want_v[0])) < 1e-3

@@ -117,3 +117,42 @@ def test_model_gpu_matches_cpu(dev):
     for n in g_c:
         err = (g_c[n] - g_g[n]).norm() / (g_c[n].norm() + 1e-8)
         assert err < 0.05, (n, err.item())
+
+
+def test_attention_output_cache_gives_same_gradients(dev):
+    """A checkpointed step that hands full-attention outputs to the recompute gives the same
+    loss as one that recomputes every attention kernel, and LoRA gradients equal up to the
+    run-to-run order of the backward's float atomics; the cache is used by the full layer."""
+    from agent_factory_3_b200.ops.attention import AttentionOutputCache, AttentionPlan
+    cfg = small_cfg()
+    lora = LoraConfig(r=8, lora_alpha=16, target_modules=["q_proj", "o_proj", "gate_up_proj"])
+    m = GptOssForCausalLM(cfg, lora=lora, device=dev).init_random(0).init_lora(1)
+    with torch.no_grad():
+        for p in m.lora_param_dict().values():
+            p.normal_(0, 0.05)
+    m.gradient_checkpointing = True
+    T = 700
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).to(dev)
+    pos = torch.cat([torch.arange(400), torch.arange(300)]).to(dev)
+    cu = torch.tensor([0, 400, 700], dtype=torch.int32)
+    labels = torch.roll(ids, -1)
+    results = []
+    for cache_bytes in (0, 1 << 30):
+        plan = AttentionPlan(cu, dev)
+        if cache_bytes:
+            plan.cache = AttentionOutputCache(cache_bytes)
+        for p in m.parameters():
+            p.grad = None
+        h = m.forward_hidden(ids, pos, cu, plan=plan)
+        lp, _ = m.token_logprobs(h, labels)
+        loss = -lp.sum()
+        loss.backward()
+        grads = [p.grad.detach().clone() for p in m.lora_param_dict().values()]
+        results.append((loss.item(), grads, plan.cache))
+    assert results[0][0] == results[1][0]
+    cache = results[1][2]
+    assert cache.hits == sum(1 for li in range(cfg.num_hidden_layers) if cfg.window(li) == 0)
+    assert cache.used == 0 and not cache.entries
+    for a, b in zip(results[0][1], results[1][1]):
+        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-3 * float(a.abs().max()) + 1e-6)

@@ -154,3 +154,54 @@ def test_sharded_optimizer_resume_through_rl_flow(tmp_path):
     for rank, ok, nonzero, steps in outs:
         assert ok and nonzero, (rank, ok, nonzero)
         assert steps == 2
+
+
+def _run_base_shard(rank, port, q):
+    """Experts sharded over the ranks (gathered on use) train exactly like replicated ones."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    try:
+        from agent_factory_3_b200.models.gpt_oss import GptOssConfig
+        from agent_factory_3_b200.trainer.model_trainer import ModelTrainer
+        from agent_factory_3_b200.trainer.training_config import TrainingConfig
+        mcfg = GptOssConfig.tiny()
+        res = {}
+        for shard in (False, True):
+            cfg = TrainingConfig(model_id="tiny", lora_r=4, lora_alpha=8,
+                                 lora_target_modules=["q_proj", "o_proj", "gate_up_proj", "down_proj"],
+                                 random_init_seed=0, use_routing_replay=False, lr_warmup_steps=0,
+                                 learning_rate=1e-2, max_capacity=256, pad_to_multiple_of_training=8,
+                                 shard_base_weights=shard, gradient_checkpointing=False)
+            tr = ModelTrainer(cfg, model_config=mcfg, device="cpu")
+            E = mcfg.num_local_experts
+            n_local = tr.model.layers[0].mlp.gate_up_blocks.shape[0]
+            losses = []
+            if rank == 0:
+                for _ in range(2):
+                    losses.append(tr.train_step(_samples(mcfg.vocab_size))["loss"])
+                tr.rpc_shutdown()
+            else:
+                tr.rpc_worker_loop()
+            flat = torch.cat([p.detach().reshape(-1) for p in tr.trainable])
+            res[shard] = (flat, losses, n_local, E)
+        q.put((rank, (res[False][0] - res[True][0]).abs().max().item(), res[False][1],
+               res[True][1], res[False][2], res[True][2], res[True][3]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_base_weights_match_replicated():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_run_base_shard, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, diff, loss_rep, loss_sh, n_rep, n_sh, E in outs:
+        assert n_rep == E and n_sh == E // 2          # each rank holds half of the experts
+        assert diff <= 1e-6, diff
+        if rank == 0:
+            assert loss_rep == loss_sh
