@@ -17,12 +17,11 @@
 //               exceeds it by more than 2^8 (then O in TMEM and the row sum are rescaled
 //               once), computes P = 2^(s*scale*log2e - m), adds P into a row sum held in
 //               registers and stores P as bf16 pairs into its TMEM lane (tcgen05.st).  The
-//               exponentials and row sums run as packed fp32x2 instructions; in blocks
-//               without masked entries a fixed share of the 2^x evaluations runs on the FMA
-//               pipe (cubic minimax polynomial after range reduction, relative error 7.5e-5,
-//               far below bf16's 2^-9) instead of the MUFU unit, which would otherwise bound
-//               the kernel: at head_dim 64 a 128x128 block needs 16384 exponentials against
-//               only 512 tensor-core clocks of MMA.
+//               scaling and row sums run as packed fp32x2 instructions.  Optionally
+//               (AF3_ATTN_POLY=2..8) a share of the 2^x evaluations of unmasked blocks runs on
+//               the FMA pipe (cubic minimax polynomial after range reduction, relative error
+//               7.5e-5, far below bf16's 2^-9) instead of the MUFU unit; measured slower on
+//               B200, so it is off by default.
 //   The sink logit joins the denominator at the end: l += 2^(sink*log2e - m).
 //   Outputs: O (bf16) and the natural-log LSE per (head, query), sink included.
 //
@@ -33,6 +32,7 @@
 // the logits, softmax, sink column dropped; models/gpt_oss in transformers); sliding window:
 // key j visible from query i iff i - j < window.
 #include <cstdlib>
+#include <string>
 
 #include "common.h"
 #include "host_utils.h"
@@ -49,7 +49,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;  // reference max moves only when exceeded by 2^8
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
-constexpr int kDefaultPoly = 6;
+// Measured on B200 (32k causal, 64q/8kv, cvt packing): 0 -> 826, 2 -> 706, 4 -> 647,
+// 6 -> 584, 8 -> 519 TFLOP/s.  The kernel is bound by softmax issue and latency, not by the MUFU unit, so moving
+// exponentials to the FMA pipe only adds instructions; the polynomial path stays selectable.
+constexpr int kDefaultPoly = 0;
 
 struct AttnFwdSmem {
   // all tiles 1024-aligned
@@ -96,9 +99,19 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+// bf16 pair of two non-negative finite floats (P values).  INT_PACK rounds on the integer
+// pipe (add half an ulp, keep the upper halves with one byte permute: round-half-up, which
+// differs from round-to-nearest-even only on exact ties), so the packing does not compete
+// with the exponentials for the conversion unit; otherwise one cvt.rn.bf16x2.f32.
+template <bool INT_PACK>
 __device__ __forceinline__ uint32_t bf16x2_of(float lo, float hi) {
   uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  if constexpr (INT_PACK) {
+    const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+    asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+  } else {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  }
   return r;
 }
 
@@ -195,7 +208,7 @@ __device__ __forceinline__ bool fwd_issue_pv(FwdIssue& t, int j, uint32_t tmem, 
 
 // POLY: number of the sixteen 8-column groups of a 128-key block whose exponentials run on
 // the FMA pipe in unmasked blocks (0 = all on the MUFU unit).
-template <int POLY>
+template <int POLY, bool INT_PACK>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qk,
                     const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
@@ -369,7 +382,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint64_t negm2 = f2_pack(-m_use, -m_use);
       // P = 2^(s * scale - m) as bf16 pairs; the row sum accumulates in two packed lanes
       uint32_t pk[kBKV / 2];
-      uint64_t rs2 = f2_pack(0.f, 0.f);
+      uint64_t rs2[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f),
+                         f2_pack(0.f, 0.f)};   // four chains: no serial add dependency
 #pragma unroll
       for (int c8 = 0; c8 < kBKV / 8; ++c8) {
         const bool poly = POLY > 0 && ((c8 * POLY) % 16) < POLY;
@@ -385,12 +399,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             e0 = ex2(x0);
             e1 = ex2(x1);
           }
-          rs2 = f2_add(rs2, f2_pack(e0, e1));
-          pk[c8 * 4 + e / 2] = bf16x2_of(e0, e1);
+          rs2[e / 2] = f2_add(rs2[e / 2], f2_pack(e0, e1));
+          pk[c8 * 4 + e / 2] = bf16x2_of<INT_PACK>(e0, e1);
         }
       }
+      const uint64_t rsa = f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3]));
       float rs0, rs1;
-      f2_unpack(rs2, rs0, rs1);
+      f2_unpack(rsa, rs0, rs1);
       l_run = l_run * alpha + (rs0 + rs1);
       // PV of the previous block must be complete before P is overwritten or O rescaled
       if (c > 0) {
@@ -504,20 +519,27 @@ void attn_fwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor tiles, torch
   p.scale_log2 = (float)scale * kLog2e;
   p.err = device_error_ptr();
   const int smem = AttnFwdSmem::TOTAL + 1024;
-  // share of the exponentials on the FMA pipe (8-column groups out of 16), AF3_ATTN_POLY
+  // share of the exponentials on the FMA pipe (8-column groups out of 16), AF3_ATTN_POLY;
+  // P packing with cvt (default) or on the integer pipe (AF3_ATTN_PACK=int).  Measured on
+  // B200 (32k causal, 64q/8kv): cvt 10.5 ms, int 11.4 ms.
   static const int poly = [] {
     const char* e = std::getenv("AF3_ATTN_POLY");
     const int v = e ? std::atoi(e) : kDefaultPoly;
-    return (v == 0 || v == 2 || v == 4 || v == 6 || v == 8) ? v : kDefaultPoly;
+    return (v == 0 || v == 4) ? v : kDefaultPoly;
   }();
-  static bool attr[64][5] = {};
+  static const bool int_pack = [] {
+    const char* e = std::getenv("AF3_ATTN_PACK");
+    return e && std::string(e) == "int";
+  }();
+  static bool attr[64][4] = {};
   int dev;
   AF3_CUDA_CHECK(cudaGetDevice(&dev));
-  auto kern = poly == 0 ? attn_fwd_kernel<0> : poly == 2 ? attn_fwd_kernel<2> :
-              poly == 4 ? attn_fwd_kernel<4> : poly == 6 ? attn_fwd_kernel<6> : attn_fwd_kernel<8>;
-  if (!attr[dev][poly / 2]) {
+  auto kern = poly == 0 ? (int_pack ? attn_fwd_kernel<0, true> : attn_fwd_kernel<0, false>)
+                        : (int_pack ? attn_fwd_kernel<4, true> : attn_fwd_kernel<4, false>);
+  const int ai = (poly ? 2 : 0) + (int_pack ? 1 : 0);
+  if (!attr[dev][ai]) {
     AF3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr[dev][poly / 2] = true;
+    attr[dev][ai] = true;
   }
   dim3 grid((unsigned)hq, (unsigned)n_tiles);
   kern<<<grid, kFwdThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, p);

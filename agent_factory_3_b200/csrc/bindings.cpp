@@ -24,6 +24,10 @@ std::tuple<torch::Tensor, pybind11::bytes> symm_alloc(int64_t nbytes, int64_t de
 int64_t ipc_open(pybind11::bytes handle);
 void ipc_close(int64_t ptr);
 void copy_from_address(int64_t src, torch::Tensor dst);
+void copy_to_address(torch::Tensor src, int64_t dst);
+void grad_signal(std::vector<int64_t> flag_ptrs, int64_t rank, int64_t epoch);
+void grad_reduce(int64_t inbox_ptr, int64_t flags_ptr, int64_t world, int64_t epoch,
+                 torch::Tensor out, torch::Tensor sumsq, double timeout_s);
 void enable_peer_access(int64_t peer);
 void tp_allreduce_norm(std::vector<int64_t> bufs, std::vector<int64_t> flags, int64_t rank,
                        int64_t epoch, int64_t ld_buf, c10::optional<torch::Tensor> residual,
@@ -95,6 +99,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &af3::symm_alloc, "zeroed cudaMalloc buffer + its CUDA IPC handle");
   m.def("ipc_open", &af3::ipc_open, "map another process's IPC buffer; returns a device pointer");
   m.def("ipc_close", &af3::ipc_close);
+  m.def("copy_to_address", &af3::copy_to_address,
+        "copy a contiguous tensor to a device address (own or peer-mapped) on the current stream");
+  m.def("grad_signal", &af3::grad_signal, "publish this rank's gradient pushes of a step");
+  m.def("grad_reduce", &af3::grad_reduce,
+        "sum the inbox slots of all ranks into the local gradient shard (+ sum of squares)");
   m.def("copy_from_address", &af3::copy_from_address,
         "copy dst.nbytes() bytes from a device address (own or peer-mapped) into dst");
   m.def("enable_peer_access", &af3::enable_peer_access,

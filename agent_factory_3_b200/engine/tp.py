@@ -219,10 +219,11 @@ class TPContext:
         dist.broadcast_object_list(obj, group=self.cpu_group, group_src=0)
         return obj[0]
 
-    def send_items(self, items: list[StepItem] | None, lora_active: bool = False) -> None:
+    def send_items(self, items: list[StepItem] | None, lora_active: bool = False,
+                   replay: bool = False) -> None:
         self.send(None if items is None else
                   ("step", [(it.ids, it.start, it.pages, it.want_logits, it.all_logits)
-                            for it in items], lora_active))
+                            for it in items], lora_active, replay))
 
     @staticmethod
     def items_of(msg) -> list[StepItem]:
@@ -250,14 +251,15 @@ class TPContext:
 
 def moe_ep_partial(xn: torch.Tensor, sh: LayerShard, n_experts: int, top_k: int, alpha: float,
                    limit: float, out: torch.Tensor, routing_out: list | None = None,
-                   lora: LoraShard | None = None) -> torch.Tensor:
+                   lora: LoraShard | None = None, replay_ids: torch.Tensor | None = None
+                   ) -> torch.Tensor:
     """This rank's share of the MoE output: sum over the token's top-k experts that live on
     this rank of gate * expert(x), written into ``out`` [T, H] (no residual).  With ``lora``
     the experts' adapters join as in the single-GPU path: x A_e^T s as extra K columns against
     the local experts' B_e rows."""
     T, H = xn.shape
     logits = G.matmul(xn, sh.router_w, bias=sh.router_b, out_dtype=torch.float32)
-    rt = M.route(logits, top_k, n_experts)
+    rt = M.route(logits, top_k, n_experts, replay_ids=replay_ids)
     if routing_out is not None:
         routing_out.append(rt.ids)
     mx = xn.is_cuda and use_cuda_kernels(xn) and sh.experts.f16_exact()
@@ -336,12 +338,17 @@ class TPModelRunner(ModelRunner):
         self.ctx.broadcast_tensors(list(self.model.lora_param_dict().values()))
         self.lora_shards = shard_lora(self.model, self.ctx.rank, self.ctx.world)
 
-    def forward(self, items: list[StepItem]) -> StepOutput:
+    def forward(self, items: list[StepItem], replay: torch.Tensor | None = None) -> StepOutput:
+        """One engine step.  ``replay`` (int [N, L, K], rank 0): expert ids to use instead of
+        the router's choice for every new token and layer (routing replay, e.g. to reproduce a
+        recorded rollout); it is broadcast to the other ranks with the step."""
         if self.lora_active and self.lora_shards is None:
             raise RuntimeError("LoRA active but not synced to the tensor-parallel ranks")
         if self.ctx.rank == 0 and self.ctx.world > 1:
-            self.ctx.send_items(items, self.lora_active)
-        return self._forward(items, self.lora_active)
+            self.ctx.send_items(items, self.lora_active, replay is not None)
+            if replay is not None:
+                self.ctx.broadcast_tensors([replay.to(self.device, torch.int32).contiguous()])
+        return self._forward(items, self.lora_active, replay)
 
     def follow(self) -> int:
         """Non-zero ranks: run the steps rank 0 broadcasts until it sends None; returns the
@@ -354,7 +361,15 @@ class TPModelRunner(ModelRunner):
             if msg[0] == "lora":
                 self._recv_lora()
                 continue
-            self._forward(TPContext.items_of(msg), bool(msg[2]))
+            items = TPContext.items_of(msg)
+            replay = None
+            if len(msg) > 3 and msg[3]:
+                cfg = self.cfg
+                replay = torch.empty(sum(len(it.ids) for it in items), cfg.num_hidden_layers,
+                                     cfg.num_experts_per_tok, device=self.device,
+                                     dtype=torch.int32)
+                self.ctx.broadcast_tensors([replay])
+            self._forward(items, bool(msg[2]), replay)
             n += 1
 
     def stop_followers(self) -> None:
@@ -362,7 +377,8 @@ class TPModelRunner(ModelRunner):
             self.ctx.send_items(None)
 
     @torch.inference_mode()
-    def _forward(self, items: list[StepItem], lora_active: bool = False) -> StepOutput:
+    def _forward(self, items: list[StepItem], lora_active: bool = False,
+                 replay: torch.Tensor | None = None) -> StepOutput:
         cfg = self.cfg
         eps = cfg.rms_norm_eps
         H = cfg.hidden_size
@@ -387,8 +403,11 @@ class TPModelRunner(ModelRunner):
             h, hn = self.ctx.allreduce_norm(part, x, sh.post_norm, eps)
             part = self.ctx.partial_buffer(m.N, H)
             lay_rec: list = []
+            rid = None
+            if replay is not None:
+                rid = replay[:, li, :].to(device=hn.device, dtype=torch.int32).contiguous()
             moe_ep_partial(hn, sh, cfg.num_local_experts, cfg.num_experts_per_tok,
-                           cfg.swiglu_alpha, cfg.swiglu_limit, part, lay_rec, lo)
+                           cfg.swiglu_alpha, cfg.swiglu_limit, part, lay_rec, lo, replay_ids=rid)
             rec.append(lay_rec[0])
             nxt = self.shards[li + 1].in_norm if li + 1 < L else None
             x, xn = self.ctx.allreduce_norm(part, h, nxt, eps)

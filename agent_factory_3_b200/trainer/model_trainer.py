@@ -144,6 +144,15 @@ class ModelTrainer(RPCMixin):
             self.shard_param = torch.nn.Parameter(self.flat_param[self.rank * S:(self.rank + 1) * S])
             self.shard_grad = torch.zeros(S, device=self.device, dtype=torch.float32)
             self.shard_param.grad = self.shard_grad
+        self.grad_pusher = None
+        if self.sharded and self.device.type == "cuda" and self.config.grad_reduce == "push":
+            # reduce-scatter by copy-engine pushes overlapped with the backward (no NCCL)
+            from ..parallel.grad_push import GradientPusher
+            offs, o = [], 0
+            for p in self.trainable:
+                offs.append(o)
+                o += p.numel()
+            self.grad_pusher = GradientPusher(self.trainable, offs, self.flat_grad, self.shard_grad)
 
     def _create_optimizer(self):
         if self.config.optimizer_type != "AdamW":
@@ -199,21 +208,32 @@ class ModelTrainer(RPCMixin):
         return sampler.plan_for_rank(self.rank)
 
     def _reduce_gradients(self):
+        """Data-parallel gradient reduction; returns this rank's shard sum of squares when the
+        reduction computed it on the way (the overlapped push path), else None."""
         if self.distributed and self.world_size > 1:
+            if self.grad_pusher is not None:
+                return self.grad_pusher.finish()
             if self.sharded:
                 dist.reduce_scatter_tensor(self.shard_grad, self.flat_grad)
             else:
                 dist.all_reduce(self.flat_grad)
+        return None
+
+    def _arm_gradient_push(self) -> None:
+        """Called before the step's last backward: gradients are pushed to their owners as
+        soon as each is final."""
+        if self.grad_pusher is not None:
+            self.grad_pusher.arm()
 
     def _apply_gradients(self) -> torch.Tensor | None:
         """Reduce, clip and apply this step's gradients; returns the global gradient norm
         (device tensor) when clipping is on."""
-        self._reduce_gradients()
+        sq_shard = self._reduce_gradients()
         g = self.shard_grad if self.sharded else self.flat_grad
         grad_norm = None
         if self.config.max_grad_norm > 0:
             if self.sharded:
-                sq = g.pow(2).sum()
+                sq = (sq_shard.reshape(()) if sq_shard is not None else g.pow(2).sum()).clone()
                 dist.all_reduce(sq)
                 grad_norm = sq.sqrt()
             else:
@@ -297,7 +317,9 @@ class ModelTrainer(RPCMixin):
         states: dict[str, MeanMetricState] = {}
         self.last_step_h2d_bytes = 0
         self.last_step_tokens = 0
-        for idx in plan:
+        for n_mb, idx in enumerate(plan):
+            if n_mb == len(plan) - 1:
+                self._arm_gradient_push()
             host = self.collator([samples[i] for i in idx])
             self.last_step_h2d_bytes += sum(v.numel() * v.element_size() for k, v in host.items()
                                             if isinstance(v, torch.Tensor) and k != "cu_seqlens")
@@ -318,6 +340,7 @@ class ModelTrainer(RPCMixin):
         self.model.train()
         batch = self._to_device(host_batch)
         loss, states = self._microbatch(batch)
+        self._arm_gradient_push()
         loss.backward()
         self._apply_gradients()
         self.step_count += 1

@@ -45,6 +45,10 @@ class TrainingConfig(BaseModel):
     # over the ranks (gradients reduce-scattered, updated shards all-gathered), the optimizer
     # state sharding of FSDP2 / ZeRO-2; the frozen base model stays replicated
     shard_optimizer_state: bool = True
+    # with the sharded optimizer on GPUs: "push" copies each gradient to its owner rank over
+    # NVLink as soon as the backward finalises it and reduces locally (parallel/grad_push.py);
+    # "nccl" runs one reduce-scatter after the backward
+    grad_reduce: Literal["push", "nccl"] = "push"
     lr_scheduler_type: LRSchedulerType = "constant_with_warmup"
     lr_warmup_steps: int = 20
     # DDIS / OPSM / entropy mask

@@ -16,14 +16,14 @@ tokens and routing), so per-GPU work is fixed as N grows.
 
 Decode (config 4, a steady-state window): 128 concurrent trajectories, each a 2048-token
 random prompt generating 8192 tokens with a 256-token random tool response appended every 1024
-generated tokens, bf16 paged KV, temperature 1.0, tensor parallel over the N GPUs.  The window
-places trajectory i at generated position 64*i (spread evenly over the 8192), prefills its
-context (prompt + generated tokens so far + the tool responses so far) untimed, then times
-every trajectory generating the next ``--decode-tokens`` tokens, tool responses included (a
-trajectory that reaches a multiple of 1024 continues as a new request on the prefix-cached
-context plus 256 tool tokens).  The window's mean context and tool-response rate are those of
-the full 8192-token run.  Then the same window with the 1-layer block-draft model proposing
-8-token blocks.
+generated tokens, bf16 paged KV, temperature 1.0, tensor parallel over the N GPUs, on the
+trained model's weights.  The window places the trajectories at generated positions spread
+evenly over the 8192, prefills their contexts (prompt + generated tokens so far + the tool
+responses so far) untimed, then times every trajectory generating the next ``--decode-tokens``
+tokens, tool responses included (a trajectory that reaches a multiple of 1024 continues as a
+new request on the prefix-cached context plus 256 tool tokens).  The window's mean context and
+tool-response rate are those of the full 8192-token run.  Then the 1-layer block-draft model
+(8-token blocks) is attached and every trajectory generates ``--spec-tokens`` more tokens.
 
     python bench.py --gpus N --steps K --warmup W            (N>1 under torch.distributed.run)
     python bench.py --impl reference ...                     (the reference's own stack)
@@ -72,6 +72,10 @@ def parse_args():
     ap.add_argument("--decode-tokens", type=int, default=256,
                     help="tokens each trajectory generates in the timed decode window")
     ap.add_argument("--no-spec", action="store_true", help="skip the block-draft decode window")
+    ap.add_argument("--spec-tokens", type=int, default=32,
+                    help="tokens each trajectory generates in the block-draft window")
+    ap.add_argument("--decode-timeout", type=float, default=600.0,
+                    help="seconds a decode window may take before it is reported incomplete")
     ap.add_argument("--trace", default=None,
                     help="after the timed steps, run one more step under torch.profiler and write "
                          "its per-kernel device-time table (text) to this path")
@@ -277,18 +281,23 @@ def run_train(args, world: int, rank: int, device):
         learning_rate=1e-5, shard_optimizer_state=not args.replicate_optimizer,
         attention_cache_gb=args.attention_cache_gb)
     BenchTrainer = bench_trainer_class()
+    from agent_factory_3_b200.trainer.model_trainer import build_model
     t_init = time.perf_counter()
-    trainer = BenchTrainer(tcfg, model_config=mcfg, device=device)
+    model = build_model(tcfg, device, mcfg)
+    trainer = BenchTrainer(tcfg, model=model, device=device)
     torch.cuda.synchronize()
     t_init = time.perf_counter() - t_init
+    log(rank, f"model + trainer ready in {t_init:.1f} s")
     if rank != 0:
         trainer.rpc_worker_loop()      # rank 0 drives every step; this rank follows
-        out = None
+        out = {}
     else:
         pool, lens = make_pool(args, world, mcfg.num_hidden_layers, mcfg.num_local_experts,
                                mcfg.num_experts_per_tok, mcfg.vocab_size, device)
+        log(rank, f"sample pool ready ({len(pool)} samples)")
         for _ in range(args.warmup):
             trainer.train_step(pool)
+        log(rank, f"{args.warmup} warm-up steps done")
         trainer.bench_sync()
         clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(device).uuid))
         clocks.start()
@@ -313,6 +322,7 @@ def run_train(args, world: int, rank: int, device):
                 f.write(prof.key_averages().table(sort_by="self_device_time_total", row_limit=60,
                                                   max_name_column_width=90))
         trainer.rpc_shutdown()
+        log(rank, f"{args.steps} timed steps done ({wall:.1f} s)")
         dev_ms = max(s["ms"] for s in stats)
         tokens = sum(s["tokens"] for s in stats)
         out = {"dev_ms": dev_ms, "wall_ms": wall * 1000.0 / args.steps, "tokens": tokens,
@@ -322,61 +332,66 @@ def run_train(args, world: int, rank: int, device):
     del trainer
     gc.collect()
     torch.cuda.empty_cache()
+    out["model"] = model        # the decode windows serve the same weights
     return out
 
 
-def run_decode(args, world: int, rank: int, device, spec: bool):
-    """One timed decode window (see the module docstring).  Rank 0 drives the engine; under
-    N>1 the other ranks follow its steps (tensor parallel)."""
+def log(rank: int, msg: str) -> None:
+    """Progress line on stderr (rank 0 only); stdout carries the one JSON line."""
+    if rank == 0:
+        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
+def run_decode(args, world: int, rank: int, device, model):
+    """The decode windows (see the module docstring) on the trained model's weights.  One
+    engine serves both: every trajectory's context is prefilled once (untimed), the plain
+    window runs, then the block draft is attached and the spec window continues the same
+    trajectories (their contexts are prefix-cache hits).  Rank 0 drives the engine; under N>1
+    the other ranks follow its steps (tensor parallel).  Returns {"plain": ..., "block_draft":
+    ...} on rank 0."""
     import numpy as np
     import torch
     import torch.distributed as dist
 
     from agent_factory_3_b200.engine.scheduler import Engine, Request
-    from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM
     from agent_factory_3_b200.ops import _ext
 
-    cfg = GptOssConfig.preset(args.model)
-    if args.layers:
-        cfg.num_hidden_layers = args.layers
-        cfg.layer_types = cfg.layer_types[: args.layers]
+    cfg = model.cfg
+    model.eval()
     R, gen_total, prompt, tool, every = args.decode_requests, 8192, 2048, 256, 1024
-    win = args.decode_tokens
-    starts = [(i * gen_total) // R for i in range(R)]
+    windows = [("plain", args.decode_tokens)]
+    if not args.no_spec:
+        windows.append(("block_draft", args.spec_tokens))
+    span = sum(w for _, w in windows)
+    starts = [(i * (gen_total - span)) // R for i in range(R)]
     ctx = [prompt + g + tool * (g // every) for g in starts]
     page = 64
     t_init = time.perf_counter()
-    model = GptOssForCausalLM(cfg, device=device).init_random(args.seed).eval()
     tp = shards = None
+    drafter = None
+    if not args.no_spec:
+        from agent_factory_3_b200.engine.spec import BlockDraftModel
+        drafter = BlockDraftModel.from_target(model, n_layers=1, block=8, seed=args.seed + 1)
     if world > 1:
-        from agent_factory_3_b200.engine.tp import TPContext, broadcast_model, shard_model
+        from agent_factory_3_b200.engine.tp import TPContext, shard_model
         cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
-        broadcast_model(model)
+        # every rank built the same random-init weights (same seed), so no broadcast is needed
         shards = shard_model(model, rank, world, free_full=True)
         torch.cuda.empty_cache()
         tp = TPContext(None, cpu_group, device, max_tokens=16384 + R * 9, hidden=cfg.hidden_size)
-    drafter = None
-    if spec:
-        from agent_factory_3_b200.engine.spec import BlockDraftModel
-        drafter = BlockDraftModel.from_target(model, n_layers=1, block=8, seed=args.seed + 1)
-    need_tokens = sum(c + win + tool * 2 + 16 for c in ctx)
+    need_tokens = sum(c + span + tool * 3 + 16 for c in ctx)
     eng = Engine(model, num_pages=need_tokens // page + 4 * R + 64, page_size=page,
                  max_running=R, max_prefill_tokens=16384, tp=tp, tp_shards=shards,
-                 drafter=drafter, max_context_tokens=prompt + gen_total + tool * 8 + 64)
+                 max_context_tokens=prompt + gen_total + tool * 8 + 64)
     torch.cuda.synchronize()
     t_init = time.perf_counter() - t_init
     if rank != 0:
         eng.runner.follow()
         tp.shutdown()
-        del eng, model
-        gc.collect()
-        torch.cuda.empty_cache()
         return None
     eng.start()
     rng = np.random.default_rng(args.seed + 7)
     lock = threading.Lock()
-    done = threading.Event()
-    state = {"left": R, "gen": 0, "requests": 0, "tool_tokens": 0}
 
     def run_batch(reqs, timeout):
         ev = threading.Event()
@@ -399,76 +414,91 @@ def run_decode(args, world: int, rank: int, device, spec: bool):
     contexts = [rng.integers(0, cfg.vocab_size, c).tolist() for c in ctx]
     pre = [Request(input_ids=c, max_new_tokens=1, temperature=1.0, seed=i, stop_token_ids=[])
            for i, c in enumerate(contexts)]
-    run_batch(pre, 3600)
+    run_batch(pre, 900)
     for c, r in zip(contexts, pre):
         c.extend(r.output_ids)
+    pos = [g + 1 for g in starts]          # generated tokens so far per trajectory
     t_pre = time.perf_counter() - t_pre
+    log(rank, f"decode: engine ready in {t_init:.1f} s, {sum(ctx)} context tokens prefilled "
+              f"in {t_pre:.1f} s")
 
-    def continue_traj(i, made):
-        """Submit trajectory i's next request: up to its next 1024 boundary, at most the
-        window's remaining tokens."""
-        pos = starts[i] + made
-        n = min(win - made, every - pos % every)
-        r = Request(input_ids=list(contexts[i]), max_new_tokens=n, temperature=1.0,
-                    seed=1000 + i * 97 + made, stop_token_ids=[])
+    def window(win: int) -> dict:
+        done = threading.Event()
+        state = {"left": R, "gen": 0, "requests": 0, "tool_tokens": 0}
 
-        def cb(out, r=r, i=i, made=made):
-            if not out["finished"]:
-                return
-            got = len(r.output_ids)
+        def continue_traj(i, made):
+            """Submit trajectory i's next request: up to its next 1024 boundary, at most the
+            window's remaining tokens."""
+            n = min(win - made, every - pos[i] % every)
+            r = Request(input_ids=list(contexts[i]), max_new_tokens=n, temperature=1.0,
+                        seed=1000 + i * 97 + pos[i], stop_token_ids=[])
+
+            def cb(out, r=r, i=i, made=made):
+                if not out["finished"]:
+                    return
+                got = len(r.output_ids)
+                with lock:
+                    state["gen"] += got
+                contexts[i].extend(r.output_ids)
+                pos[i] += got
+                total = made + got
+                if total >= win or got == 0 or r.finish_reason.get("type") == "abort":
+                    with lock:
+                        state["left"] -= 1
+                        if state["left"] == 0:
+                            done.set()
+                    return
+                if pos[i] % every == 0:      # the tool call returns 256 tokens
+                    contexts[i].extend(rng.integers(0, cfg.vocab_size, tool).tolist())
+                    with lock:
+                        state["tool_tokens"] += tool
+                continue_traj(i, total)
+            r.on_output = cb
             with lock:
-                state["gen"] += got
-            contexts[i].extend(r.output_ids)
-            total = made + got
-            if total >= win or r.finish_reason.get("type") == "abort":
-                with lock:
-                    state["left"] -= 1
-                    if state["left"] == 0:
-                        done.set()
-                return
-            if (starts[i] + total) % every == 0:      # tool call returns 256 tokens
-                contexts[i].extend(rng.integers(0, cfg.vocab_size, tool).tolist())
-                with lock:
-                    state["tool_tokens"] += tool
-            continue_traj(i, total)
-        r.on_output = cb
-        with lock:
-            state["requests"] += 1
-        eng.submit(r)
+                state["requests"] += 1
+            eng.submit(r)
 
-    torch.cuda.synchronize()
-    l0 = _ext.launch_count()
-    t0 = time.perf_counter()
-    for i in range(R):
-        continue_traj(i, 0)
-    ok = done.wait(1800)
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
-    launches = _ext.launch_count() - l0
-    eng.stop()
-    err = None
+        torch.cuda.synchronize()
+        l0 = _ext.launch_count()
+        t0 = time.perf_counter()
+        for i in range(R):
+            continue_traj(i, 0)
+        ok = done.wait(args.decode_timeout)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        res = {"tok_per_s": round(state["gen"] / wall, 1) if ok else None, "completed": ok,
+               "generated_tokens": state["gen"], "window_s": round(wall, 2),
+               "requests": state["requests"], "tool_tokens_prefilled": state["tool_tokens"],
+               "window_tokens_per_trajectory": win,
+               "mean_context": round(float(np.mean([len(c) for c in contexts])) - win / 2, 1),
+               "launches_rank0": _ext.launch_count() - l0}
+        return res
+
+    out = {"prefill_setup_s": round(t_pre, 1), "init_s": round(t_init, 1)}
     try:
-        _ext.check_device_error()
-    except Exception as e:  # noqa: BLE001
-        err = str(e)[:200]
-    res = {"tok_per_s": round(state["gen"] / wall, 1) if ok else None, "completed": ok,
-           "generated_tokens": state["gen"], "window_s": round(wall, 2),
-           "requests": state["requests"], "tool_tokens_prefilled": state["tool_tokens"],
-           "prefill_setup_s": round(t_pre, 1), "init_s": round(t_init, 1),
-           "mean_context": round(float(np.mean(ctx)) + win / 2, 1), "launches_rank0": launches}
-    if drafter is not None:
-        res["spec"] = {"draft": "1-layer random-init block draft", "block": 8,
-                       "accept_length": round(eng.spec_accept_length, 3),
-                       "accept_rate": round(eng.spec_accept_rate, 4),
-                       "verifies": eng.spec_verifies}
-    if err:
-        res["device_error"] = err
-    if tp is not None:
-        tp.shutdown()
-    del eng, model
-    gc.collect()
-    torch.cuda.empty_cache()
-    return res
+        for name, win in windows:
+            if name == "block_draft":
+                eng.drafter = drafter
+            res = window(win)
+            if name == "block_draft":
+                res["spec"] = {"draft": "1-layer random-init block draft (acceptance is near "
+                                        "zero with random weights; this times the machinery)",
+                               "block": 8, "accept_length": round(eng.spec_accept_length, 3),
+                               "accept_rate": round(eng.spec_accept_rate, 4),
+                               "verifies": eng.spec_verifies}
+            out[name] = res
+            log(rank, f"decode window {name}: {res['tok_per_s']} tok/s in {res['window_s']} s")
+            if not res["completed"]:
+                break
+    finally:
+        eng.stop()
+        try:
+            _ext.check_device_error()
+        except Exception as e:  # noqa: BLE001
+            out["device_error"] = str(e)[:200]
+        if tp is not None:
+            tp.shutdown()
+    return out
 
 
 def main():
@@ -489,16 +519,14 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
 
     tr = run_train(args, world, rank, device)
+    model = tr.pop("model")
     decode = None
     if not args.no_decode:
-        decode = {}
-        for spec in ((False,) if args.no_spec else (False, True)):
-            try:
-                r = run_decode(args, world, rank, device, spec)
-            except Exception as e:  # noqa: BLE001 - the training number still stands
-                r = {"error": f"{type(e).__name__}: {e}"[:300]}
-            if rank == 0:
-                decode["block_draft" if spec else "plain"] = r
+        try:
+            decode = run_decode(args, world, rank, device, model)
+        except Exception as e:  # noqa: BLE001 - the training number still stands
+            decode = {"error": f"{type(e).__name__}: {e}"[:300]}
+    del model
     if rank == 0:
         total_tokens = tr["tokens"]
         value = total_tokens / (tr["dev_ms"] / 1000.0)
@@ -545,9 +573,8 @@ def main():
         if decode is not None:
             d = {"metric": "rollout decode tok/s (config 4 steady-state window, whole job)",
                  "tp": world, "requests": args.decode_requests,
-                 "window_tokens_per_trajectory": args.decode_tokens,
-                 "timing": "host clock around the window; engine idle and device synchronised "
-                           "at both ends", **decode}
+                 "timing": "host clock around each window; engine idle and device "
+                           "synchronised at both ends", **decode}
             out["decode"] = d
         print(json.dumps(out), flush=True)
     if world > 1:

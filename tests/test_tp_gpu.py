@@ -127,7 +127,9 @@ def _run_engine(rank, port, q):
                 ref = ModelRunner(model, kv(1), lora_active=active)
                 for items in steps:
                     w_out = ref.forward(items)
-                    g_out = runner.forward(items)
+                    # the TP runner replays the single-GPU run's experts, so both compute the
+                    # same function and only the bf16 rounding of the partial sums differs
+                    g_out = runner.forward(items, replay=w_out.routing)
                     want, got = w_out.logits, g_out.logits
                     res.append(((got - want).abs().mean().item(), want.abs().mean().item(),
                                 float((got.argmax(-1) == want.argmax(-1)).float().mean()),
@@ -157,11 +159,9 @@ def test_tp2_runner_matches_single_gpu():
         p.join(timeout=60)
     assert outs[1] == 4
     assert len(outs[0]) == 4
-    # bf16 partial sums round differently from the single-GPU epilogue, and the random-init
-    # router has near-ties, so routed experts flip for a few percent of (token, layer) slots and
-    # those tokens' logits move.  Measured on 2 x B200: mean |diff| 1.6 % of mean |logit| on decode
-    # steps, 13 % on prefill with 96 % of routed experts equal.  The check bounds that; exact
-    # equality needs the two runners to share routing (replay), which they do not yet.
+    # With the single-GPU routing replayed, the two runners compute the same function; the TP
+    # path rounds each rank's partial sum to bf16 before the all-reduce while the single-GPU
+    # epilogue rounds once, which bounds the difference to a few bf16 ulps per layer.
     for mean_err, mean_scale, agree, max_err, route_agree in outs[0]:
-        assert mean_err <= 0.2 * mean_scale, outs[0]
-        assert route_agree >= 0.85, outs[0]
+        assert route_agree == 1.0, outs[0]
+        assert mean_err <= 0.03 * mean_scale, outs[0]
