@@ -77,31 +77,71 @@ __device__ __forceinline__ void pack8(const float* v, uint32_t& a, uint32_t& b, 
   d = pack_bf16x2(v[6], v[7]);
 }
 
-// P^T and dS^T of one key row over 32 query columns starting at c.  lse2 (log2 domain) and D
-// of the block's queries are in shared memory at lds (lse2[128] then D[128]); every lane reads
-// the same addresses, so the 16-byte loads are broadcasts.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_of(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// P^T and dS^T of one key row over 16 query columns starting at c, as bf16 pairs (packed
+// fp32x2 arithmetic).  lse2 (log2 domain) and D of the block's queries are in shared memory at
+// lds (lse2[128] then D[128]); every lane reads the same addresses, so the 16-byte loads are
+// broadcasts.
 template <bool MASK>
-__device__ __forceinline__ void softmax_grad_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32],
-                                                   const float* lds, int c, float scale_log2,
-                                                   int key, int qb, int k1, int q_end, int window,
-                                                   float (&pr)[32], float (&dsr)[32]) {
+__device__ __forceinline__ void softmax_grad16(const uint32_t (&sv)[16], const uint32_t (&dv)[16],
+                                               const float* lds, int c, float scale_log2, int key,
+                                               int qb, int k1, int q_end, int window,
+                                               uint32_t (&pp)[8], uint32_t (&dd)[8]) {
+  const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
-  for (int e4 = 0; e4 < 8; ++e4) {
+  for (int e4 = 0; e4 < 4; ++e4) {
     const float4 l4 = *reinterpret_cast<const float4*>(lds + c + e4 * 4);
     const float4 d4 = *reinterpret_cast<const float4*>(lds + kB + c + e4 * 4);
-    const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e4 * 4 + u;
-      float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[u]));
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int e = e4 * 4 + h2 * 2;
+      const float la = h2 ? l4.z : l4.x, lb = h2 ? l4.w : l4.y;
+      const float da = h2 ? d4.z : d4.x, db = h2 ? d4.w : d4.y;
+      float t0, t1;
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc2,
+                       f2_pack(-la, -lb)), t0, t1);
+      float p0 = ex2(t0), p1 = ex2(t1);
       if (MASK) {
-        const int qi = qb + c + e;
-        const bool vis = key < k1 && key <= qi && qi < q_end && (window == 0 || qi - key < window);
-        pv = vis ? pv : 0.f;
+        const int q0 = qb + c + e, q1 = q0 + 1;
+        const bool v0 = key < k1 && key <= q0 && q0 < q_end && (window == 0 || q0 - key < window);
+        const bool v1 = key < k1 && key <= q1 && q1 < q_end && (window == 0 || q1 - key < window);
+        p0 = v0 ? p0 : 0.f;
+        p1 = v1 ? p1 : 0.f;
       }
-      pr[e] = pv;
-      dsr[e] = pv * (__uint_as_float(dv[e]) - dd[u]);
+      float s0, s1;
+      f2_unpack(f2_mul(f2_pack(p0, p1),
+                       f2_add(f2_pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+                              f2_pack(-da, -db))), s0, s1);
+      pp[e / 2] = bf16x2_of(p0, p1);
+      dd[e / 2] = bf16x2_of(s0, s1);
     }
   }
 }
@@ -331,32 +371,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qb = k0 + (it % nqb) * kB;
       const uint32_t pt = smem_u32(smem + Smem::PT + (it & 1) * kB * kB * 2);
       const uint32_t ds = smem_u32(smem + Smem::DST + (it & 1) * kB * kB * 2);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = hf * 64 + cc * 32;  // query column of this 32-wide chunk
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lb + c, sv);
-        tmem_ld_32x32b_x32(tmem + lb + 128 + c, dv);
-        tmem_ld_wait();
-        if (cc == 1) {
-          tc_fence_before();
-          mbar_arrive(&s_empty[hf]);
-        }
-        // every query of this chunk visible from this key row?
-        const bool all_vis = key < k1 && key <= qb + c && qb + c + 31 < q_end &&
-                             (p.window == 0 || qb + c + 31 - key < p.window);
-        float pr[32], dsr[32];
-        if (all_vis)
-          softmax_grad_chunk<false>(sv, dv, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pr, dsr);
-        else
-          softmax_grad_chunk<true>(sv, dv, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pr, dsr);
+      // four 16-query chunks; the TMEM loads of chunk q+1 are in flight while chunk q computes
+      uint32_t sA[16], dA[16], sB[16], dB[16];
+      tmem_ld_32x32b_x16(tmem + lb + hf * 64, sA);
+      tmem_ld_32x32b_x16(tmem + lb + 128 + hf * 64, dA);
+      tmem_ld_wait();
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          uint32_t a, b, cw, d;
-          pack8(&pr[q8 * 8], a, b, cw, d);
-          store_sw128(pt, r, c / 8 + q8, a, b, cw, d);
-          pack8(&dsr[q8 * 8], a, b, cw, d);
-          store_sw128(ds, r, c / 8 + q8, a, b, cw, d);
+      for (int q = 0; q < 4; ++q) {
+        const int c = hf * 64 + q * 16;  // query column of this chunk
+        if (q < 3) {
+          if (q % 2 == 0) {
+            tmem_ld_32x32b_x16(tmem + lb + c + 16, sB);
+            tmem_ld_32x32b_x16(tmem + lb + 128 + c + 16, dB);
+          } else {
+            tmem_ld_32x32b_x16(tmem + lb + c + 16, sA);
+            tmem_ld_32x32b_x16(tmem + lb + 128 + c + 16, dA);
+          }
+        }
+        const bool all_vis = key < k1 && key <= qb + c && qb + c + 15 < q_end &&
+                             (p.window == 0 || qb + c + 15 - key < p.window);
+        uint32_t pp[8], dd[8];
+        if (q % 2 == 0) {
+          if (all_vis)
+            softmax_grad16<false>(sA, dA, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
+          else
+            softmax_grad16<true>(sA, dA, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
+        } else {
+          if (all_vis)
+            softmax_grad16<false>(sB, dB, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
+          else
+            softmax_grad16<true>(sB, dB, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
+        }
+        store_sw128(pt, r, c / 8, pp[0], pp[1], pp[2], pp[3]);
+        store_sw128(pt, r, c / 8 + 1, pp[4], pp[5], pp[6], pp[7]);
+        store_sw128(ds, r, c / 8, dd[0], dd[1], dd[2], dd[3]);
+        store_sw128(ds, r, c / 8 + 1, dd[4], dd[5], dd[6], dd[7]);
+        if (q < 3) {
+          tmem_ld_wait();
+          if (q == 2) {   // every S^T / dP^T column of this half is in registers
+            tc_fence_before();
+            mbar_arrive(&s_empty[hf]);
+          }
         }
       }
       mbar_arrive(&ld_empty[s]);

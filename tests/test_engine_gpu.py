@@ -2,8 +2,10 @@
 sliding window, GQA), KV page store/gather, Gumbel-max sampling statistics, and greedy engine
 decoding equal to a full recompute on the GPU model."""
 import asyncio
+import base64
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -95,13 +97,19 @@ def test_engine_greedy_gpu(dev):
         eng.stop()
     # Teacher-forced check against a full recompute: a random-init model has near-tied logits
     # (top-2 gaps of a few 1e-3), so compare each greedy token with the recomputed logits at
-    # its position instead of comparing token sequences.
+    # its position instead of comparing token sequences.  Its router has near-ties too: the
+    # recompute replays the experts the engine reported (R3), so a routing flip between the
+    # decode path and the packed forward cannot move the logits.
     out = a["output_ids"]
     assert len(out) == 8, a
     ids = prompt + out[:-1]
+    routed = np.frombuffer(base64.b64decode(a["meta_info"]["routed_experts"]), dtype=np.int32)
+    routed = torch.from_numpy(routed.reshape(len(ids), cfg.num_hidden_layers,
+                                             cfg.num_experts_per_tok).copy())
     with torch.no_grad():
         h = model.forward_hidden(torch.tensor(ids, device=dev), torch.arange(len(ids), device=dev),
-                                 torch.tensor([0, len(ids)], dtype=torch.int32))
+                                 torch.tensor([0, len(ids)], dtype=torch.int32),
+                                 routing_indices=routed.to(dev))
         lg = model.logits(h[len(prompt) - 1:]).float()
     chosen = lg[torch.arange(8, device=dev), torch.tensor(out, device=dev)]
     assert bool((chosen >= lg.max(-1).values - 0.05).all()), (out, lg.argmax(-1).tolist())

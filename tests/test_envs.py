@@ -182,3 +182,69 @@ def test_serper_search_with_fake_http():
     r = _call(srv, "scrape_webpage", {"url": "https://a"})
     assert r["text"] == "y" * 10 and r["truncated"]
     assert "error" in _call(SS.build_server(api_key=""), "search", {"q": "x"})
+
+
+# ---------------------------------------------------------------- seccomp sandbox + stress
+def test_seccomp_program_layout():
+    from agent_factory_3_b200.envs import seccomp as SC
+    prog = SC.program()
+    assert prog[-1] == (0x06, 0, 0, SC.RET_ERRNO | SC.EPERM)        # the shared DENY return
+    deny = len(prog) - 1
+    for i, (code, jt, jf, k) in enumerate(prog):
+        if code in (0x15, 0x35, 0x45):                            # conditional jumps
+            assert 0 <= i + 1 + jt < len(prog) and jf == 0
+        if code == 0x15 and k in SC.DENIED.values():
+            assert i + 1 + jt == deny
+    assert len(SC.program_bytes()) == 8 * len(prog)
+
+
+@pytest.mark.skipif(not __import__("agent_factory_3_b200.envs.seccomp", fromlist=["x"]).available(),
+                    reason="seccomp filters unavailable in this container")
+def test_seccomp_lockdown_denies_network_exec_and_writes(tmp_path):
+    import subprocess
+    import sys
+
+    from agent_factory_3_b200.envs import seccomp as SC
+    target = tmp_path / "x.txt"
+    code = SC.INSTALL_SNIPPET + f"""
+_af3_lockdown({SC.program_bytes().hex()!r})
+import os, socket, threading
+res = []
+for name, fn in [("socket", lambda: socket.socket()), ("write", lambda: open({str(target)!r}, "w")),
+                 ("exec", lambda: os.execv("/bin/true", ["true"])),
+                 ("mkdir", lambda: os.mkdir({str(tmp_path / 'd')!r}))]:
+    try:
+        fn(); res.append(name + ":allowed")
+    except OSError as e:
+        res.append(name + ":" + str(e.errno))
+t = threading.Thread(target=lambda: None); t.start(); t.join()
+print(" ".join(res), open("/proc/self/status").read().count("Seccomp"))
+"""
+    r = subprocess.run([sys.executable, "-I", "-c", code], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.split()[:4] == ["socket:1", "write:1", "exec:1", "mkdir:1"], r.stdout
+    assert not target.exists()
+
+
+@pytest.mark.skipif(not __import__("agent_factory_3_b200.envs.seccomp", fromlist=["x"]).available(),
+                    reason="seccomp filters unavailable in this container")
+def test_python_sandbox_seccomp_session():
+    s = PS.PythonSession(timeout=20, use_seccomp=True)
+    try:
+        assert s.run("x = 20\nx + 1")["result"] == "21"
+        r = s.run("import socket\ntry:\n    socket.socket()\n    print('net')\n"
+                  "except OSError as e:\n    print('denied', e.errno)\nx * 2")
+        assert r["stdout"].strip() == "denied 1" and r["result"] == "40"
+        r = s.run("try:\n    open('out.txt', 'w')\nexcept OSError as e:\n    print('denied', e.errno)")
+        assert r["stdout"].strip() == "denied 1"
+    finally:
+        s.stop()
+
+
+def test_sandbox_stress_local():
+    from agent_factory_3_b200.envs import seccomp as SC
+    from agent_factory_3_b200.envs import sandbox_stress as ST
+    rep = ST.run_local(12, 4, seed=1, timeout=30, use_seccomp=SC.available(), use_bwrap=False)
+    s = rep.summary()
+    assert s["total"] == 12 and s["success"] == 12 and s["steps"] == 36, s
+    assert s["latency_s"]["p50"] is not None
