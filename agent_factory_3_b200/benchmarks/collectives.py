@@ -5,7 +5,10 @@
     baseline doing the same work (``all_reduce`` of the partial, then residual add + RMSNorm);
   * ``weight_sync``: the fused fp32 -> bf16 cast + NVLink store of trainer tensors (rank 1) into
     rank 0's staging buffer against NCCL ``send``/``recv`` of the same bf16 bytes after a
-    separate cast.
+    separate cast;
+  * ``grad_rs``: the trainer's pushed gradient reduce-scatter against NCCL reduce-scatter;
+  * ``expert_gather``: the fused NVLink gather + MXFP4 dequantisation of sharded experts
+    against NCCL all-gather + dequantisation.
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m agent_factory_3_b200.benchmarks.collectives --op allreduce
 
@@ -130,9 +133,103 @@ def bench_weight_sync(a, rank, world, dev):
     return rows
 
 
+def bench_grad_rs(a, rank, world, dev):
+    """Data-parallel gradient reduce-scatter: the trainer's push path (every rank copies each
+    owner's slice into the owner's IPC inbox with the copy engines, then one kernel waits for
+    all ranks and sums the slots in rank order, with the sum of squares) against NCCL
+    ``reduce_scatter_tensor`` of the same fp32 buffer.  Here the pushes are not overlapped with
+    a backward pass (the trainer issues them during it), so this is the exposed worst case."""
+    from ..ops._ext import check_device_error
+    from ..parallel.grad_push import GradientPusher
+    rows = []
+    for mb in a.sizes_mb:
+        S = int(mb * 1e6 / 4 / world) // 64 * 64           # fp32 elements per rank's slice
+        flat = torch.randn(world * S, device=dev)
+        shard = torch.empty(S, device=dev)
+        dummy = torch.zeros(1, device=dev, requires_grad=True)
+        pusher = GradientPusher([dummy], [0], flat, shard, timeout_s=60.0)
+        pusher.ranges = [(0, world * S)]                   # the whole buffer is one tensor
+        pusher.pushed = [False]
+        ref = torch.empty(S, device=dev)
+
+        def push():
+            pusher.finish()
+
+        def nccl():
+            dist.reduce_scatter_tensor(ref, flat)
+
+        t_push = _max_over_ranks(_time(push, a.iters))
+        t_nccl = _max_over_ranks(_time(nccl, a.iters))
+        torch.cuda.synchronize()
+        err = (shard - ref).abs().max().item()
+        nbytes = world * S * 4
+        # every rank sends (W-1)/W of its buffer and receives as much
+        roof = (world - 1) * S * 4 / (LINK_GBS * 1e9) * 1e3
+        rows.append({"bytes": nbytes, "push_ms": round(t_push, 4), "nccl_rs_ms": round(t_nccl, 4),
+                     "speedup_vs_nccl": round(t_nccl / t_push, 2),
+                     "nvlink_roofline_ms": round(roof, 4), "push_frac_of_roofline": round(roof / t_push, 3),
+                     "nccl_frac_of_roofline": round(roof / t_nccl, 3), "max_abs_diff_vs_nccl": err})
+        pusher.check()
+        pusher.close()
+        dist.barrier()
+    check_device_error()
+    return rows
+
+
+def bench_expert_gather(a, rank, world, dev):
+    """Sharded frozen experts: one gpt-oss-120b layer's gate_up experts (128 x 5760 x 2880
+    MXFP4) rebuilt as bf16 on every rank.  Fused: ``mxfp4_dequant_gather`` reads every owner's
+    packed bytes and scales over NVLink and writes bf16 locally.  Baseline: NCCL all-gather of
+    the packed bytes and scales, then the local dequantisation kernel."""
+    from ..ops import mxfp4
+    from ..ops._ext import check_device_error, ext
+    from ..parallel.symm import PeerMappedBuffer
+    E, N, K = 128, 5760, 2880
+    epr = E // world
+    nb, ns = epr * N * (K // 32) * 16, epr * N * (K // 32)
+    off_s = (nb + 255) // 256 * 256
+    buf = PeerMappedBuffer(off_s + ns, None, dev)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    blocks_l = buf.local[:nb].view(epr, N, K // 32, 16)
+    scales_l = buf.local[off_s:off_s + ns].view(epr, N, K // 32)
+    blocks_l.copy_(torch.randint(0, 256, blocks_l.shape, generator=g, device=dev, dtype=torch.uint8))
+    scales_l.copy_(torch.randint(118, 128, scales_l.shape, generator=g, device=dev, dtype=torch.uint8))
+    torch.cuda.synchronize()
+    dist.barrier()
+    tabs = (torch.tensor(list(buf.bases), dtype=torch.int64, device=dev),
+            torch.tensor([b + off_s for b in buf.bases], dtype=torch.int64, device=dev))
+    out = torch.empty(E, N, K, device=dev, dtype=torch.bfloat16)
+    full_b = torch.empty(E, N, K // 32, 16, device=dev, dtype=torch.uint8)
+    full_s = torch.empty(E, N, K // 32, device=dev, dtype=torch.uint8)
+
+    def fused():
+        ext().mxfp4_dequant_gather(tabs[0], tabs[1], epr, out)
+
+    def nccl():
+        dist.all_gather_into_tensor(full_b, blocks_l)
+        dist.all_gather_into_tensor(full_s, scales_l)
+        mxfp4.dequantize(full_b, full_s, out=out)
+
+    t_fused = _max_over_ranks(_time(fused, a.iters))
+    t_nccl = _max_over_ranks(_time(nccl, a.iters))
+    packed = E * N * K // 2 + E * N * K // 32
+    link_ms = (world - 1) / world * packed / (LINK_GBS * 1e9) * 1e3
+    hbm_ms = (E * N * K * 2 + packed / world) / 6541.5e9 * 1e3
+    roof = max(link_ms, hbm_ms)
+    row = {"layer_packed_bytes": packed, "fused_ms": round(t_fused, 4),
+           "nccl_ag_dequant_ms": round(t_nccl, 4), "speedup_vs_nccl": round(t_nccl / t_fused, 2),
+           "roofline_ms": round(roof, 4), "roofline_bound": "nvlink" if link_ms > hbm_ms else "hbm",
+           "frac_of_roofline": round(roof / t_fused, 3)}
+    check_device_error()
+    dist.barrier()
+    buf.close()
+    return [row]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["allreduce", "weight_sync"], default="allreduce")
+    ap.add_argument("--op", choices=["allreduce", "weight_sync", "grad_rs", "expert_gather"],
+                    default="allreduce")
     ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 32, 128, 512, 2048, 8192])
     ap.add_argument("--hidden", type=int, default=2880)
     ap.add_argument("--sizes-mb", type=float, nargs="+", default=[1, 16, 64, 256, 1024])
@@ -143,8 +240,9 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     try:
-        rows = bench_allreduce(a, rank, world, dev) if a.op == "allreduce" else \
-            bench_weight_sync(a, rank, world, dev)
+        rows = {"allreduce": bench_allreduce, "weight_sync": bench_weight_sync,
+                "grad_rs": bench_grad_rs, "expert_gather": bench_expert_gather}[a.op](
+                    a, rank, world, dev)
         if rank == 0:
             for r in rows:
                 print(json.dumps({"op": a.op, "world": world, **r}), flush=True)

@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--replicate-optimizer", action="store_true",
                     help="keep the whole AdamW state on every rank (one all-reduce) instead of "
                          "the default sharded optimizer state")
+    ap.add_argument("--grad-reduce", choices=["push", "nccl"], default="nccl",
+                    help="data-parallel gradient reduce-scatter: one NCCL reduce-scatter after "
+                         "the backward (default) or copy-engine pushes overlapped with it")
     ap.add_argument("--attention-cache-gb", type=float, default=12.0,
                     help="GB of full-attention outputs kept for the checkpoint recompute")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode window")
@@ -279,7 +282,7 @@ def run_train(args, world: int, rank: int, device):
         max_capacity=args.tokens, pad_to_multiple_of_training=1024, random_init_seed=0,
         use_routing_replay=True, gradient_checkpointing=True, lr_warmup_steps=0,
         learning_rate=1e-5, shard_optimizer_state=not args.replicate_optimizer,
-        attention_cache_gb=args.attention_cache_gb)
+        attention_cache_gb=args.attention_cache_gb, grad_reduce=args.grad_reduce)
     BenchTrainer = bench_trainer_class()
     from agent_factory_3_b200.trainer.model_trainer import build_model
     t_init = time.perf_counter()
@@ -555,6 +558,7 @@ def main():
                        "routing_replay": True, "activation_checkpointing": True,
                        "attention_cache_gb": args.attention_cache_gb,
                        "optimizer": "replicated" if args.replicate_optimizer else "sharded",
+                       "grad_reduce": args.grad_reduce if world > 1 else None,
                        "parallelism": f"dp{world}" if world > 1 else "single",
                        "layers": tr["layers"],
                        "l2": "inputs larger than L2 (65 GB of weights stream every step)"},
