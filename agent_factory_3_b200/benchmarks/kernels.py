@@ -99,6 +99,13 @@ def bench_gemm(args):
     from ..ops import gemm as G
     a = torch.randn(args.m, args.k, device="cuda").bfloat16()
     b = torch.randn(args.n, args.k, device="cuda").bfloat16()
+    if getattr(args, "dtype", "bf16") == "fp8":
+        from ..ops import fp8
+        aq, asc = fp8.quant_rows(a)
+        bq, _ = fp8.quant_rows(b)
+        one = torch.ones(1, device="cuda")
+        ms = _time(lambda: fp8.matmul_f8(aq, asc, bq, one), args.iters)
+        return {"flops": 2 * args.m * args.n * args.k, "ms": ms}
     out = torch.empty(args.m, args.n, device="cuda").bfloat16()
     ms = _time(lambda: G.matmul(a, b, out=out), args.iters)
     return {"flops": 2 * args.m * args.n * args.k, "ms": ms}
@@ -115,6 +122,16 @@ def bench_moe(args):
     xs = M.gather_rows(x, rt.row_src)
     W = (torch.randn(E, 2 * I, H, device="cuda") * 0.02).bfloat16()
     bias = torch.zeros(E, 2 * I, device="cuda")
+    if getattr(args, "dtype", "bf16") == "fp8":
+        # e4m3 operands (kind::f8f6f4): the GEMM alone, operands quantised once outside
+        from ..ops import fp8
+        xq, xsc = fp8.quant_rows(xs)
+        Wq, _ = fp8.quant_rows(W.reshape(E * 2 * I, H))
+        Wq = Wq.reshape(E, 2 * I, H)
+        es = torch.ones(E, device="cuda")
+        ms = _time(lambda: fp8.grouped_matmul_f8(xq, xsc, Wq, es, rt.offsets, epilogue="swiglu",
+                                                 bias=bias), args.iters)
+        return {"flops": 2 * T * K * 2 * I * H, "ms": ms}
     ms = _time(lambda: G.grouped_matmul(xs, W, rt.offsets, epilogue="swiglu", bias=bias), args.iters)
     return {"flops": 2 * T * K * 2 * I * H, "ms": ms}
 
@@ -198,6 +215,8 @@ def bench_peer_sync(args):
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--dtype", choices=["bf16", "fp8"], default="bf16",
+                    help="operand type of the GEMM (--op gemm / moe)")
     ap.add_argument("--op", required=True, choices=["attn_fwd", "attn_bwd", "gemm", "moe", "dequant", "moe_decode",
                                                   "peer_sync", "decode_attn"])
     ap.add_argument("--seqlens", default="8192")

@@ -14,7 +14,8 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           c10::optional<torch::Tensor> lse_part, c10::optional<torch::Tensor> label_logit,
           c10::optional<torch::Tensor> row_stats, int64_t n_tiles_total, int64_t bn,
           int64_t band, int64_t out_group_stride, int64_t max_ctas,
-          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2);
+          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2,
+          c10::optional<torch::Tensor> acc_add);
 void mxfp4_dequant(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out);
 void mxfp4_dequant_gather(torch::Tensor block_ptrs, torch::Tensor scale_ptrs,
                           int64_t experts_per_rank, torch::Tensor out);
@@ -25,6 +26,18 @@ int64_t ipc_open(pybind11::bytes handle);
 void ipc_close(int64_t ptr);
 void copy_from_address(int64_t src, torch::Tensor dst);
 void copy_to_address(torch::Tensor src, int64_t dst);
+void mxfp4_to_e4m3(torch::Tensor blocks, torch::Tensor scales, torch::Tensor out,
+                   torch::Tensor expert_scale);
+void transpose_u8(torch::Tensor in, torch::Tensor out);
+void quant_rows_e4m3(torch::Tensor x, torch::Tensor out, torch::Tensor scale);
+void gemm_f8(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi, int64_t sched,
+             int64_t M, int64_t N, int64_t K, c10::optional<torch::Tensor> group_offsets,
+             int64_t num_groups, torch::Tensor a_scale, torch::Tensor b_scale,
+             c10::optional<torch::Tensor> bias, int64_t bias_group_stride,
+             c10::optional<torch::Tensor> row_scale, c10::optional<torch::Tensor> aux,
+             c10::optional<torch::Tensor> out2, c10::optional<torch::Tensor> acc_add,
+             double alpha, double act_alpha, double act_limit, int64_t bn, int64_t band,
+             int64_t max_ctas);
 void grad_signal(std::vector<int64_t> flag_ptrs, int64_t rank, int64_t epoch);
 void grad_reduce(int64_t inbox_ptr, int64_t flags_ptr, int64_t world, int64_t epoch,
                  torch::Tensor out, torch::Tensor sumsq, double timeout_s);
@@ -90,7 +103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("labels"), py::arg("vocab_offset"), py::arg("lse_part"),
         py::arg("label_logit"), py::arg("row_stats"), py::arg("n_tiles_total"), py::arg("bn"),
         py::arg("band"), py::arg("out_group_stride"), py::arg("max_ctas"),
-        py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("K2") = 0);
+        py::arg("a2") = py::none(), py::arg("b2") = py::none(), py::arg("K2") = 0,
+        py::arg("acc_add") = py::none());
   m.def("mxfp4_dequant", &af3::mxfp4_dequant);
   m.def("mxfp4_dequant_gather", &af3::mxfp4_dequant_gather,
         "MXFP4 -> bf16 of an expert stack sharded over peer-mapped per-rank buffers");
@@ -99,6 +113,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &af3::symm_alloc, "zeroed cudaMalloc buffer + its CUDA IPC handle");
   m.def("ipc_open", &af3::ipc_open, "map another process's IPC buffer; returns a device pointer");
   m.def("ipc_close", &af3::ipc_close);
+  m.def("mxfp4_to_e4m3", &af3::mxfp4_to_e4m3,
+        "MXFP4 experts -> e4m3 bytes [E, N, K] + one fp32 scale per expert");
+  m.def("transpose_u8", &af3::transpose_u8, "[G, R, C] -> [G, C, R] bytes");
+  m.def("quant_rows_e4m3", &af3::quant_rows_e4m3, "bf16 rows -> e4m3 + per-row fp32 scale");
+  m.def("gemm_f8", &af3::gemm_f8, "tcgen05 kind::f8f6f4 GEMM (e4m3, K-major) with scaled epilogues");
   m.def("copy_to_address", &af3::copy_to_address,
         "copy a contiguous tensor to a device address (own or peer-mapped) on the current stream");
   m.def("grad_signal", &af3::grad_signal, "publish this rank's gradient pushes of a step");

@@ -15,7 +15,8 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
           c10::optional<torch::Tensor> lse_part, c10::optional<torch::Tensor> label_logit,
           c10::optional<torch::Tensor> row_stats, int64_t n_tiles_total, int64_t bn,
           int64_t band, int64_t out_group_stride, int64_t max_ctas,
-          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2) {
+          c10::optional<torch::Tensor> a2, c10::optional<torch::Tensor> b2, int64_t K2,
+          c10::optional<torch::Tensor> acc_add) {
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
   AF3_CHECK(a.dim() == 2 && a.stride(1) == 1, "a must be 2-D with unit inner stride");
@@ -86,6 +87,14 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
   args.row_stats = row_stats.has_value() ? row_stats->data_ptr<float>() : nullptr;
   args.n_tiles_total = (int)n_tiles_total;
   args.err = device_error_ptr();
+  if (acc_add.has_value()) {
+    check_cuda_bf16(*acc_add, "acc_add");
+    AF3_CHECK(acc_add->dim() == 2 && acc_add->stride(1) == 1 && acc_add->size(0) >= M &&
+                  acc_add->size(1) >= N && acc_add->stride(0) % 8 == 0,
+              "acc_add must be bf16 [M, N] with unit inner stride and 16-byte rows");
+    args.acc_add = reinterpret_cast<const __nv_bfloat16*>(acc_add->data_ptr());
+    args.ld_acc_add = acc_add->stride(0);
+  }
 
   if (sched != kSchedPlain) {
     AF3_CHECK(group_offsets.has_value(), "grouped GEMM needs group_offsets");

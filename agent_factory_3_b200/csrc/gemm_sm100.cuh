@@ -10,6 +10,11 @@
 //   device from the segment offsets, so no host synchronisation is needed.
 // * Grouped-K mode: the reduction runs over segment g's rows only and the output is C[g]
 //   (weight gradients of per-expert LoRA factors).
+// * FP8 variant (template flag F8): A and B are e4m3 bytes, K-major, and the MMA runs as
+//   tcgen05 kind::f8f6f4 (32 K elements per instruction, twice the bf16 rate).  A stage still
+//   holds 128-byte rows, now 128 K elements, so tiles, swizzle and descriptors are unchanged.
+//   The epilogue multiplies the accumulator by a per-row scale of A (per-token quantisation)
+//   and a per-group scale of B (per-expert weight scale) before everything else.
 //
 // Warp roles (256 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected
 // thread), warp 2 = TMEM allocator, warps 4..7 = epilogue (thread t owns accumulator row t;
@@ -65,6 +70,15 @@ struct GemmArgs {
   const float* row_stats;    // backward: [M, 4] = (logZ, H, g_logprob, g_entropy)
   int n_tiles_total;
   int* err;                  // device error word
+  // FP8 dequantisation scales (either may be null) and an optional bf16 term added to the
+  // scaled accumulator before bias and epilogue (a second GEMM's result, e.g. the base output
+  // of an FP8 pass under a bf16 LoRA pass)
+  const float* a_scale;      // [M] per row of A
+  const float* b_scale;      // [G] per group (per expert) of B
+  const __nv_bfloat16* acc_add;
+  int64_t ld_acc_add;
+  int kx_shift;              // K-major x coordinate = k >> kx_shift (FP8 bytes described as
+                             // 16-bit elements to the TMA unit: 1)
 };
 
 template <int BN>
@@ -141,10 +155,13 @@ __device__ __forceinline__ bool get_tile(int t, const GemmArgs& a, int BN, const
   return true;
 }
 
+// sigmoid through the fast reciprocal (__fdividef): the IEEE division would cost a
+// multi-instruction sequence per element in the epilogue, which for e4m3 tiles (half the
+// main-loop time of bf16) otherwise becomes the limiter
 __device__ __forceinline__ float silu_clamped_fwd(float g, float u, float alpha, float limit) {
   const float gc = fminf(g, limit);
   const float uc = fminf(fmaxf(u, -limit), limit);
-  const float s = 1.0f / (1.0f + __expf(-alpha * gc));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-alpha * gc));
   return gc * s * (uc + 1.0f);
 }
 
@@ -152,7 +169,7 @@ __device__ __forceinline__ void silu_clamped_bwd(float dout, float g, float u, f
                                                  float limit, float& dg, float& du) {
   const float gc = fminf(g, limit);
   const float uc = fminf(fmaxf(u, -limit), limit);
-  const float s = 1.0f / (1.0f + __expf(-alpha * gc));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-alpha * gc));
   const float glu = gc * s;
   du = (u >= -limit && u <= limit) ? dout * glu : 0.0f;
   const float dglu = dout * (uc + 1.0f);
@@ -199,11 +216,42 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, int row, bool row_o
     return;
   }
   if (!row_ok) return;
+  if (a.a_scale != nullptr || a.b_scale != nullptr) {
+    const float sc = (a.a_scale != nullptr ? a.a_scale[row] : 1.f) *
+                     (a.b_scale != nullptr ? a.b_scale[g] : 1.f);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= sc;
+  }
+  if (a.acc_add != nullptr) {
+    const __nv_bfloat16* ap = a.acc_add + (int64_t)row * a.ld_acc_add + col0;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w = *reinterpret_cast<const uint4*>(ap + q * 8);
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[q * 8 + e] += __bfloat162float(h[e]);
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < a.N) v[j] += __bfloat162float(ap[j]);
+    }
+  }
   if (a.bias != nullptr) {
     const float* bp = a.bias + (int64_t)g * a.bias_group_stride + col0;
+    if (full && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || col0 + j < a.N) v[j] += bp[j];
+      for (int q = 0; q < 8; ++q) {
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(bp) + q);
+        v[4 * q] += b4.x;
+        v[4 * q + 1] += b4.y;
+        v[4 * q + 2] += b4.z;
+        v[4 * q + 3] += b4.w;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < a.N) v[j] += bp[j];
+    }
   }
   if (EPI == kEpiBf16 || EPI == kEpiRowScale) {
     if (EPI == kEpiRowScale) {
@@ -351,7 +399,7 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, int row, bool row_o
 // DUAL: after the main K loop, K2 more columns are reduced from a second operand pair
 // (A2, B2) with the same majors -- e.g. the LoRA branch [x | s*x*A^T] x [W | B]^T of a
 // LoRA-adapted linear layer runs as one GEMM.
-template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI, bool DUAL>
+template <int BN, bool A_MN, bool B_MN, bool B_3D, int SCHED, int EPI, bool DUAL, bool F8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
@@ -359,6 +407,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       const __grid_constant__ CUtensorMap tma_b2, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  static_assert(!F8 || (!A_MN && !B_MN && !DUAL), "FP8 operands are K-major, single pair");
+  constexpr int KB = F8 ? 128 : kBK;   // K elements per stage (128 bytes per row either way)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -441,7 +491,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       TileCoord tc;
       for (int t = blockIdx.x; get_tile<SCHED>(t, args, BN, prefix, tc); t += gridDim.x) {
-        const int nk1 = (tc.k_end - tc.k_begin + kBK - 1) / kBK;
+        const int nk1 = (tc.k_end - tc.k_begin + KB - 1) / KB;
         const int nk = nk1 + (DUAL ? (args.K2 + kBK - 1) / kBK : 0);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
@@ -450,18 +500,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const bool second = DUAL && kb >= nk1;
           const CUtensorMap* ma = second ? &tma_a2 : &tma_a;
           const CUtensorMap* mb = second ? &tma_b2 : &tma_b;
-          const int k = second ? (kb - nk1) * kBK : tc.k_begin + kb * kBK;
+          const int k = second ? (kb - nk1) * kBK : tc.k_begin + kb * KB;
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          const int kx = F8 ? (k >> args.kx_shift) : k;
           if (!A_MN) {
-            tma_load_2d(sa, ma, &full_bar[stage], k, tc.m0);
+            tma_load_2d(sa, ma, &full_bar[stage], kx, tc.m0);
           } else {
 #pragma unroll
             for (int c = 0; c < kBM / 64; ++c)
               tma_load_2d(sa + c * 8192, ma, &full_bar[stage], tc.m0 + c * 64, k);
           }
           if (!B_MN) {
-            if (B_3D) tma_load_3d(sb, mb, &full_bar[stage], k, tc.n0, tc.g);
-            else tma_load_2d(sb, mb, &full_bar[stage], k, tc.n0);
+            if (B_3D) tma_load_3d(sb, mb, &full_bar[stage], kx, tc.n0, tc.g);
+            else tma_load_2d(sb, mb, &full_bar[stage], kx, tc.n0);
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c) {
@@ -477,7 +528,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ================================ MMA issuer ======================================
     if (elect_one_sync()) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc =
+          F8 ? make_idesc_e4m3(kBM, BN) : make_idesc_bf16(kBM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
@@ -489,7 +541,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * BN;
         uint32_t accum = 0;
         bool ok = true;
-        const int nk = (tc.k_end - tc.k_begin + kBK - 1) / kBK +
+        const int nk = (tc.k_end - tc.k_begin + KB - 1) / KB +
                        (DUAL ? (args.K2 + kBK - 1) / kBK : 0);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, args.err, abort_flag)) { ok = false; break; }
@@ -502,7 +554,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                      : make_smem_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
             const uint64_t bd = B_MN ? make_smem_desc(sb + kk * 2048, 8192, 1024, kLayoutSW128)
                                      : make_smem_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
-            umma_f16(d_tmem, ad, bd, idesc, accum);
+            if (F8) umma_f8(d_tmem, ad, bd, idesc, accum);
+            else umma_f16(d_tmem, ad, bd, idesc, accum);
             accum = 1;
           }
           umma_commit(&empty_bar[stage]);

@@ -144,7 +144,8 @@ class GptOssMoE(nn.Module):
     def experts(self) -> ExpertWeights:
         return ExpertWeights(self.gate_up_blocks, self.gate_up_scales, self.gate_up_bias,
                              self.down_blocks, self.down_scales, self.down_bias,
-                             shards=getattr(self, "expert_shards", None))
+                             shards=getattr(self, "expert_shards", None),
+                             dequant_dtype=getattr(self, "dequant_dtype", "bf16"))
 
     def forward(self, xn, residual, replay_ids=None, routing_out=None):
         cfg = self.cfg

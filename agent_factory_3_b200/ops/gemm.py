@@ -36,11 +36,11 @@ def _call(a, a_mn, b, b_mn, out, epi, sched, M, N, K, *, offsets=None, num_group
           bias_gstride=0, row_scale=None, aux=None, out2=None, alpha=1.0, beta=0.0,
           act_alpha=SWIGLU_ALPHA, act_limit=SWIGLU_LIMIT, labels=None, vocab_offset=0,
           lse_part=None, label_logit=None, row_stats=None, n_tiles_total=0, bn=256, band=8,
-          out_group_stride=0, max_ctas=0, a2=None, b2=None, K2=0):
+          out_group_stride=0, max_ctas=0, a2=None, b2=None, K2=0, acc_add=None):
     ext().gemm(a, a_mn, b, b_mn, out, epi, sched, M, N, K, offsets, num_groups, bias,
                bias_gstride, row_scale, aux, out2, float(alpha), float(beta), float(act_alpha),
                float(act_limit), labels, vocab_offset, lse_part, label_logit, row_stats,
-               n_tiles_total, bn, band, out_group_stride, max_ctas, a2, b2, K2)
+               n_tiles_total, bn, band, out_group_stride, max_ctas, a2, b2, K2, acc_add)
 
 
 def _as_mk(a: torch.Tensor, layout: str) -> torch.Tensor:
@@ -146,7 +146,7 @@ def swiglu_reference(gate_up: torch.Tensor, alpha=SWIGLU_ALPHA, limit=SWIGLU_LIM
 
 def grouped_matmul_reference(a, b, offsets, b_layout="nk", epilogue="bf16", bias=None,
                              row_scale=None, aux=None, alpha=1.0, act_alpha=SWIGLU_ALPHA,
-                             act_limit=SWIGLU_LIMIT, a2=None, b2=None):
+                             act_limit=SWIGLU_LIMIT, a2=None, b2=None, acc_add=None):
     """Reference of :func:`grouped_matmul`; returns (out, out2)."""
     R = a.shape[0]
     N = b.shape[1] if b_layout == "nk" else b.shape[2]
@@ -160,6 +160,8 @@ def grouped_matmul_reference(a, b, offsets, b_layout="nk", epilogue="bf16", bias
             w2 = b2[g].float()
             y = y + a2[s:e].float() @ (w2.t() if b_layout == "nk" else w2)
         y = y * alpha
+        if acc_add is not None:
+            y = y + acc_add[s:e].float()
         if bias is not None:
             y = y + bias[g].float()
         res[s:e] = y
@@ -190,7 +192,8 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
                    out2: torch.Tensor | None = None, alpha: float = 1.0,
                    act_alpha: float = SWIGLU_ALPHA, act_limit: float = SWIGLU_LIMIT,
                    save_preact: bool = False, bn: int | None = None, band: int = 4,
-                   a2: torch.Tensor | None = None, b2: torch.Tensor | None = None):
+                   a2: torch.Tensor | None = None, b2: torch.Tensor | None = None,
+                   acc_add: torch.Tensor | None = None):
     """Per-expert GEMM over the expert-sorted, 128-row padded activation buffer.
 
     a: [R, K] sorted rows; b: [G, N, K] ("nk") or [G, K, N] ("kn"); offsets: int32 [G+1]
@@ -200,11 +203,13 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
       * ``swiglu``: columns interleaved (gate, up) -> out = clamped SwiGLU [R, N/2]; with
         ``save_preact`` the raw gate_up is also written to ``out2`` [R, N]
       * ``swiglu_bwd``: acc = dL/dh, aux = raw gate_up [R, 2N] -> out = dL/d(gate_up) [R, 2N]
+    ``acc_add`` (bf16 [R, N]) is added to alpha*acc before bias and epilogue: the result of
+    another GEMM over the same rows (e.g. an FP8 base product under a bf16 LoRA product).
     Returns (out, out2).
     """
     if not use_cuda_kernels(a, b):
         o, o2 = grouped_matmul_reference(a, b, offsets, b_layout, epilogue, bias, row_scale, aux,
-                                         alpha, act_alpha, act_limit, a2, b2)
+                                         alpha, act_alpha, act_limit, a2, b2, acc_add)
         if out is not None:
             out.copy_(o)
             o = out
@@ -236,7 +241,7 @@ def grouped_matmul(a: torch.Tensor, b: torch.Tensor, offsets: torch.Tensor, *,
           bias=bias, bias_gstride=(bias.stride(0) if bias is not None else 0),
           row_scale=row_scale, aux=aux, out2=out2 if epi == EPI_SWIGLU else None, alpha=alpha,
           act_alpha=act_alpha, act_limit=act_limit, bn=bn, band=band, a2=a2, b2=b2,
-          K2=(a2.shape[1] if dual else 0))
+          K2=(a2.shape[1] if dual else 0), acc_add=acc_add)
     return out, (out2 if epi == EPI_SWIGLU else None)
 
 

@@ -36,21 +36,49 @@ class ExpertWeights:
 
     _scratch: dict = {}
 
-    def __init__(self, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, shards=None):
+    def __init__(self, gu_blocks, gu_scales, gu_bias, dn_blocks, dn_scales, dn_bias, shards=None,
+                 dequant_dtype: str = "bf16"):
         self.gu_blocks, self.gu_scales, self.gu_bias = gu_blocks, gu_scales, gu_bias
         self.dn_blocks, self.dn_scales, self.dn_bias = dn_blocks, dn_scales, dn_bias
         # parallel.fsdp.ExpertShards when the blocks / scales above are only this rank's
         # experts; the full stack is then gathered (fused with the dequantisation) on use
         self.shards = shards
+        # "bf16": training GEMMs on bf16 dequantised experts; "fp8": e4m3 experts with one
+        # scale per expert, e4m3 activations with one scale per row (ops/fp8.py)
+        if dequant_dtype not in ("bf16", "fp8"):
+            raise ValueError(f"dequant_dtype must be 'bf16' or 'fp8', got {dequant_dtype!r}")
+        if dequant_dtype == "fp8" and shards is not None:
+            raise ValueError("the fp8 expert mode is not available with sharded experts")
+        self.dequant_dtype = dequant_dtype
 
     @classmethod
-    def _buf(cls, key, shape, device):
-        k = (key, tuple(shape), str(device))
+    def _buf(cls, key, shape, device, dtype=torch.bfloat16):
+        k = (key, tuple(shape), str(device), dtype)
         b = cls._scratch.get(k)
         if b is None:
-            b = torch.empty(shape, device=device, dtype=torch.bfloat16)
+            b = torch.empty(shape, device=device, dtype=dtype)
             cls._scratch[k] = b
         return b
+
+    def _e4m3(self, which: str, blocks, scales, transposed: bool):
+        """(e4m3 [E, N, K] -- or [E, K, N] when ``transposed`` --, fp32 scale [E])."""
+        from . import fp8
+        E, N, Gk, _ = blocks.shape
+        dev = blocks.device
+        cuda = blocks.is_cuda
+        w = self._buf(which + "8", (E, N, Gk * 32), dev, torch.uint8) if cuda else None
+        sc = self._buf(which + "8s", (E,), dev, torch.float32) if cuda else None
+        w, sc = fp8.mxfp4_to_e4m3(blocks, scales, out=w, expert_scale=sc)
+        if not transposed:
+            return w, sc
+        wt = self._buf(which + "8t", (E, Gk * 32, N), dev, torch.uint8) if cuda else None
+        return fp8.transpose_u8(w, out=wt), sc
+
+    def gate_up_e4m3(self, transposed: bool = False):
+        return self._e4m3("gu", self.gu_blocks, self.gu_scales, transposed)
+
+    def down_e4m3(self, transposed: bool = False):
+        return self._e4m3("dn", self.dn_blocks, self.dn_scales, transposed)
 
     def _dequantized(self, which: str, blocks, scales) -> torch.Tensor:
         E, N, Gk, _ = self.shards.shapes[which + "_blocks"] if self.shards else blocks.shape
@@ -127,6 +155,9 @@ class MoEFn(torch.autograd.Function):
         lora_gu = gu_A is not None
         lora_dn = dn_A is not None
         need_grad = torch.is_grad_enabled() or any(ctx.needs_input_grad)
+        if experts.dequant_dtype == "fp8":
+            return MoEFn._forward_fp8(ctx, xn, residual, rt, x_s, gu_A, gu_B, dn_A, dn_B, experts,
+                                      top_k, s, act_alpha, act_limit, need_grad)
         W_gu = experts.gate_up()
         xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if lora_gu else None
         h, gu = G.grouped_matmul(x_s, W_gu, rt.offsets, epilogue="swiglu", bias=experts.gu_bias,
@@ -146,7 +177,93 @@ class MoEFn(torch.autograd.Function):
         return out
 
     @staticmethod
+    def _forward_fp8(ctx, xn, residual, rt, x_s, gu_A, gu_B, dn_A, dn_B, experts, top_k, s,
+                     act_alpha, act_limit, need_grad):
+        """Expert GEMMs on e4m3 operands.  The LoRA branches stay bf16 and run as a second
+        GEMM over the same rows that adds the e4m3 base product (``acc_add``) before the fused
+        epilogue."""
+        from . import fp8
+        lora_gu, lora_dn = gu_A is not None, dn_A is not None
+        x_q, x_sc = fp8.quant_rows(x_s)
+        W_gu, s_gu = experts.gate_up_e4m3()
+        xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if lora_gu else None
+        if lora_gu:
+            base, _ = fp8.grouped_matmul_f8(x_q, x_sc, W_gu, s_gu, rt.offsets,
+                                            bias=experts.gu_bias)
+            h, gu = G.grouped_matmul(xa, _b(gu_B), rt.offsets, epilogue="swiglu",
+                                     act_alpha=act_alpha, act_limit=act_limit,
+                                     save_preact=need_grad, acc_add=base)
+            del base
+        else:
+            h, gu = fp8.grouped_matmul_f8(x_q, x_sc, W_gu, s_gu, rt.offsets, epilogue="swiglu",
+                                          bias=experts.gu_bias, act_alpha=act_alpha,
+                                          act_limit=act_limit, save_preact=need_grad)
+        del x_q
+        h_q, h_sc = fp8.quant_rows(h)
+        W_dn, s_dn = experts.down_e4m3()
+        ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if lora_dn else None
+        if lora_dn:
+            base, _ = fp8.grouped_matmul_f8(h_q, h_sc, W_dn, s_dn, rt.offsets,
+                                            bias=experts.dn_bias)
+            y_s, _ = G.grouped_matmul(ha, _b(dn_B), rt.offsets, epilogue="rowscale",
+                                      row_scale=rt.row_gate, acc_add=base)
+            del base
+        else:
+            y_s, _ = fp8.grouped_matmul_f8(h_q, h_sc, W_dn, s_dn, rt.offsets, epilogue="rowscale",
+                                           bias=experts.dn_bias, row_scale=rt.row_gate)
+        out = M.combine_rows(y_s, rt.dest, top_k, residual=residual)
+        ctx.experts = experts
+        ctx.cfg = (top_k, s, act_alpha, act_limit, lora_gu, lora_dn)
+        ctx.rt = rt
+        ctx.save_for_backward(xn, gu_A, gu_B, dn_A, dn_B, xa, h, ha, gu)
+        return out
+
+    @staticmethod
+    def _backward_fp8(ctx, dout):
+        from . import fp8
+        xn, gu_A, gu_B, dn_A, dn_B, xa, h, ha, gu = ctx.saved_tensors
+        top_k, s, act_alpha, act_limit, lora_gu, lora_dn = ctx.cfg
+        rt = ctx.rt
+        experts = ctx.experts
+        dout = dout.contiguous()
+        g = M.gather_rows(dout, rt.row_src, rt.row_gate)            # gate * dout, [R, H]
+        g_q, g_sc = fp8.quant_rows(g)
+        W_dnT, s_dn = experts.down_e4m3(transposed=True)            # [E, I, H]: dh = g W_dn
+        d_dnA = d_dnB = d_guA = d_guB = None
+        if lora_dn:
+            gd = G.grouped_matmul(g, _b(dn_B), rt.offsets, b_layout="kn", alpha=s)[0]  # [R, r]
+            base, _ = fp8.grouped_matmul_f8(g_q, g_sc, W_dnT, s_dn, rt.offsets)
+            dgu, _ = G.grouped_matmul(gd, _b(dn_A), rt.offsets, b_layout="kn",
+                                      epilogue="swiglu_bwd", aux=gu, act_alpha=act_alpha,
+                                      act_limit=act_limit, acc_add=base)
+            del base
+            d_dnA = G.grouped_k_matmul(gd, h, rt.offsets)                   # [E, r, I]
+            d_dnB = G.grouped_k_matmul(g, ha, rt.offsets)                   # [E, H, r]
+        else:
+            dgu, _ = fp8.grouped_matmul_f8(g_q, g_sc, W_dnT, s_dn, rt.offsets,
+                                           epilogue="swiglu_bwd", aux=gu, act_alpha=act_alpha,
+                                           act_limit=act_limit)
+        del g, g_q
+        d_q, d_sc = fp8.quant_rows(dgu)
+        W_guT, s_gu = experts.gate_up_e4m3(transposed=True)         # [E, H, 2I]: dx = dgu W_gu
+        if lora_gu:
+            ga = G.grouped_matmul(dgu, _b(gu_B), rt.offsets, b_layout="kn", alpha=s)[0]
+            base, _ = fp8.grouped_matmul_f8(d_q, d_sc, W_guT, s_gu, rt.offsets)
+            dx_s, _ = G.grouped_matmul(ga, _b(gu_A), rt.offsets, b_layout="kn", acc_add=base)
+            del base
+            x_s = M.gather_rows(xn, rt.row_src)
+            d_guA = G.grouped_k_matmul(ga, x_s, rt.offsets)                 # [E, r, H]
+            d_guB = G.grouped_k_matmul(dgu, xa, rt.offsets)                 # [E, 2I, r]
+        else:
+            dx_s, _ = fp8.grouped_matmul_f8(d_q, d_sc, W_guT, s_gu, rt.offsets)
+        dxn = M.combine_rows(dx_s, rt.dest, top_k)
+        return (dxn, dout, None, None, d_guA, d_guB, d_dnA, d_dnB, None, None, None, None, None,
+                None, None)
+
+    @staticmethod
     def backward(ctx, dout):
+        if ctx.experts.dequant_dtype == "fp8":
+            return MoEFn._backward_fp8(ctx, dout)
         xn, gu_A, gu_B, dn_A, dn_B, xa, h, ha, gu = ctx.saved_tensors
         top_k, s, act_alpha, act_limit, lora_gu, lora_dn = ctx.cfg
         rt = ctx.rt

@@ -66,6 +66,8 @@ def build_model(config: TrainingConfig, device, model_config: GptOssConfig | Non
     else:
         model.init_random(seed=config.random_init_seed or 0)
     model.gradient_checkpointing = config.gradient_checkpointing
+    for layer in model.layers:
+        layer.mlp.dequant_dtype = config.dequant_dtype
     model.attention_cache_bytes = int(config.attention_cache_gb * 1e9)
     if config.training_mode == "full":
         for n, p in model.named_parameters():

@@ -51,6 +51,10 @@ class TrainingConfig(BaseModel):
     # with gpt-oss-120b (131k tokens per GPU): 19.4 s per step with "nccl", 21.9 s with "push"
     # -- the pushes' HBM and NVLink traffic slows the backward more than the overlap saves
     grad_reduce: Literal["push", "nccl"] = "nccl"
+    # expert GEMMs of training: "bf16" dequantised experts, or "fp8" (e4m3 experts with one
+    # scale per expert, e4m3 activations and gradients with one scale per row; the
+    # reference's quantizer_config.dequant_dtype)
+    dequant_dtype: Literal["bf16", "fp8"] = "bf16"
     lr_scheduler_type: LRSchedulerType = "constant_with_warmup"
     lr_warmup_steps: int = 20
     # DDIS / OPSM / entropy mask
