@@ -1,7 +1,12 @@
-"""Sokoban (text observations) as an MCP environment (reference environment:
-mcp_tools/sokoban/server_text.py:63-380 over gym_sokoban, with its deadlock detector under
-mcp_tools/sokoban/deadlock_detector).  The image server of the reference renders PIL frames on
-the CPU; this environment serves the text board only.
+"""Sokoban as an MCP environment with text or image observations (reference environments:
+mcp_tools/sokoban/server_text.py:63-380 over gym_sokoban with its deadlock detector under
+mcp_tools/sokoban/deadlock_detector, and the image server mcp_tools/sokoban/server.py:19-190).
+
+* Image mode (``build_server(..., image=True)``, ``--image``): every observation is a frame
+  drawn on the CPU with numpy (16-pixel tiles, nearest-neighbour upscaled by 1.75 as in the
+  reference) and sent as a JPEG image block; the tool result is [description, image(s),
+  metadata], the metadata as a fenced ``metadata`` JSON text block (the reference's format,
+  which the rollout executor reads as structured output).
 
 * Levels come from our own generator: a room is carved by a random walk inside a wall border,
   targets are placed on floor cells, and the start position is made by playing the game
@@ -201,9 +206,72 @@ class SokobanGame:
                 "move_history": list(self.history), "difficulty": self.level.difficulty, **extra}
 
 
-def build_server(width: int = 7, height: int = 7, num_boxes: int = 2, seed: int | None = None):
-    """FastMCP server with ``get_init_state`` and ``move_sequence`` over one game."""
+# ------------------------------------------------------------------ image observations
+TILE = 16
+UPSCALE = 1.75
+_COLORS = {"wall": (96, 64, 48), "floor": (24, 24, 24), "target": (200, 40, 40),
+           "box": (220, 170, 40), "box_on_target": (60, 190, 60), "player": (70, 130, 230)}
+
+
+def _tile(kind: str, on_target: bool):
+    import numpy as np
+    t = np.empty((TILE, TILE, 3), np.uint8)
+    t[:] = _COLORS["wall" if kind == "wall" else "floor"]
+    if kind == "wall":
+        t[::4, :] = (72, 48, 36)                       # brick courses
+        return t
+    if on_target:                                      # red outline of the target square
+        t[2:14, 2:4] = t[2:14, 12:14] = _COLORS["target"]
+        t[2:4, 2:14] = t[12:14, 2:14] = _COLORS["target"]
+    if kind == "box":
+        t[3:13, 3:13] = _COLORS["box_on_target" if on_target else "box"]
+        t[7:9, 3:13] = t[3:13, 7:9] = (90, 60, 20)     # box cross-beams
+    elif kind == "player":
+        yy, xx = np.mgrid[0:TILE, 0:TILE]
+        t[(yy - 7.5) ** 2 + (xx - 7.5) ** 2 <= 20] = _COLORS["player"]
+    return t
+
+
+def render_frame(level: SokobanLevel, upscale: float = UPSCALE):
+    """RGB uint8 [H, W, 3] frame of the board (numpy tiles, nearest-neighbour upscale)."""
+    import numpy as np
+    img = np.empty((level.h * TILE, level.w * TILE, 3), np.uint8)
+    for y in range(level.h):
+        for x in range(level.w):
+            c = (x, y)
+            on_t = c in level.targets
+            kind = ("wall" if c in level.walls else "player" if c == level.player
+                    else "box" if c in level.boxes else "floor")
+            img[y * TILE:(y + 1) * TILE, x * TILE:(x + 1) * TILE] = _tile(kind, on_t)
+    if upscale != 1.0:
+        H, W = int(img.shape[0] * upscale), int(img.shape[1] * upscale)
+        ys = (np.arange(H) / upscale).astype(int)
+        xs = (np.arange(W) / upscale).astype(int)
+        img = img[ys][:, xs]
+    return img
+
+
+def frame_jpeg(level: SokobanLevel, quality: int = 90) -> bytes:
+    import io
+
+    from PIL import Image as PILImage
+    buf = io.BytesIO()
+    PILImage.fromarray(render_frame(level)).save(buf, format="JPEG", quality=quality)
+    return buf.getvalue()
+
+
+def metadata_block(meta: dict) -> str:
+    import json
+    return f"```metadata\n{json.dumps(meta, indent=2)}\n```"
+
+
+def build_server(width: int = 7, height: int = 7, num_boxes: int = 2, seed: int | None = None,
+                 image: bool = False):
+    """FastMCP server with ``get_init_state`` and ``move_sequence`` over one game (text board,
+    or JPEG frames with ``image``)."""
     from mcp.server.fastmcp import FastMCP
+    if image:
+        return _build_image_server(width, height, num_boxes, seed)
 
     game = SokobanGame(width, height, num_boxes, seed)
     mcp = FastMCP(name="sokoban", instructions=(
@@ -251,6 +319,57 @@ def build_server(width: int = 7, height: int = 7, num_boxes: int = 2, seed: int 
     return mcp
 
 
+def _build_image_server(width: int, height: int, num_boxes: int, seed: int | None):
+    from mcp.server.fastmcp import FastMCP, Image
+
+    game = SokobanGame(width, height, num_boxes, seed)
+    mcp = FastMCP(name="sokoban-image", instructions=(
+        "Sokoban: push every yellow box onto a red-outlined target (a box on a target turns "
+        "green). You are the blue circle; brown cells are walls. Call get_init_state to see the "
+        f"board, then move_sequence with up to {game.max_moves_per_call} directions "
+        "(up, down, left, right) per call."))
+
+    @mcp.tool(description="Return the current board as an image (call once at the start).")
+    def get_init_state() -> list:
+        meta = game.meta(early_exit=False, is_passed=False, is_deadlock=False)
+        return ["Sokoban game initialized. Ready to play! Use move_sequence to make moves.",
+                Image(data=frame_jpeg(game.level), format="jpeg"), metadata_block(meta)]
+
+    @mcp.tool(description="Make up to 5 moves in order; an image after each move; stops early "
+                          "on a solve or a deadlock.")
+    def move_sequence(directions: Annotated[list[str], "moves, e.g. [\"up\", \"left\"] (max 5)"]) -> list:
+        if len(directions) > game.max_moves_per_call:
+            return [f"Error: Maximum {game.max_moves_per_call} moves allowed, got {len(directions)}.",
+                    metadata_block(game.meta(early_exit=False, is_passed=False, is_deadlock=False))]
+        if game.done:
+            return ["Error: Game already completed.",
+                    metadata_block(game.meta(early_exit=True, is_passed=True, is_deadlock=False))]
+        out: list = []
+        passed, deadlock = False, []
+        for d in directions:
+            d = str(d).lower()
+            if d not in DIRS:
+                out.append(f"Error: invalid direction '{d}'. Valid directions: {sorted(DIRS)}")
+                break
+            _, pushed, solved = game.step(d)
+            if pushed:
+                deadlock = find_deadlocks(game.level, game.live)
+            if solved:
+                out.append("Congratulations! You solved the puzzle!")
+                passed = True
+                break
+            out += [f"Step {game.steps}, Move: {d}", Image(data=frame_jpeg(game.level), format="jpeg")]
+            if deadlock:
+                out.append("Deadlock detected!\n" + "\n".join(f"  - {r}" for r in deadlock))
+                break
+        out.append(metadata_block(game.meta(early_exit=passed or bool(deadlock), is_passed=passed,
+                                            is_deadlock=bool(deadlock))))
+        return out
+
+    mcp.game = game
+    return mcp
+
+
 def reward(result, metadata: dict) -> float:
     """1.0 for a solved puzzle, else 0.0."""
     for s in reversed(getattr(result, "steps", []) if result is not None else []):
@@ -266,8 +385,9 @@ def main():
     ap.add_argument("--height", type=int, default=7)
     ap.add_argument("--boxes", type=int, default=2)
     ap.add_argument("--seed", type=int, default=None)
+    ap.add_argument("--image", action="store_true", help="JPEG frame observations")
     a = ap.parse_args()
-    build_server(a.width, a.height, a.boxes, a.seed).run()
+    build_server(a.width, a.height, a.boxes, a.seed, image=a.image).run()
 
 
 if __name__ == "__main__":

@@ -191,6 +191,16 @@ class McpExecutor:
             if isinstance(structured, dict) and "result" in structured and len(structured) == 1 \
                     and isinstance(structured["result"], dict):
                 structured = structured["result"]
+            if not structured:
+                # a fenced ```metadata``` JSON text block (servers that mix text and images)
+                for t in texts:
+                    st = t.strip()
+                    if st.startswith("```metadata") and st.endswith("```"):
+                        try:
+                            parsed = json.loads(st[len("```metadata"):-3])
+                            structured = parsed if isinstance(parsed, dict) else {}
+                        except ValueError:
+                            pass
             if not structured and len(texts) == 1:
                 # servers that return a JSON object only as text: treat it as structured
                 try:

@@ -248,3 +248,53 @@ def test_sandbox_stress_local():
     s = rep.summary()
     assert s["total"] == 12 and s["success"] == 12 and s["steps"] == 36, s
     assert s["latency_s"]["p50"] is not None
+
+
+# ---------------------------------------------------------------- sokoban image observations
+def test_sokoban_frame_tiles():
+    rows = ["XXXXX",
+            "X@B.X",
+            "X..TX",
+            "XXXXX"]
+    walls = {(x, y) for y, r in enumerate(rows) for x, ch in enumerate(r) if ch == "X"}
+    lv = SK.SokobanLevel(walls, {(3, 2)}, {(2, 1)}, (1, 1), 5, 4)
+    img = SK.render_frame(lv, upscale=1.0)
+    assert img.shape == (4 * SK.TILE, 5 * SK.TILE, 3)
+    c = SK.TILE // 2
+
+    def px(x, y):
+        return tuple(int(v) for v in img[y * SK.TILE + c, x * SK.TILE + c])
+    assert px(1, 1) == SK._COLORS["player"]
+    assert px(2, 1) == (90, 60, 20) or px(2, 1) == SK._COLORS["box"]
+    assert px(3, 1) == SK._COLORS["floor"]
+    assert img[2 * SK.TILE + 2, 3 * SK.TILE + 2].tolist() == list(SK._COLORS["target"])
+    big = SK.render_frame(lv)
+    assert big.shape[:2] == (int(4 * SK.TILE * SK.UPSCALE), int(5 * SK.TILE * SK.UPSCALE))
+
+
+def test_sokoban_image_server_and_metadata_block():
+    import base64
+    import io
+
+    from PIL import Image as PILImage
+
+    from agent_factory_3_b200.rollout.mcp_executor import McpExecutor
+    srv = SK.build_server(7, 7, 2, seed=4, image=True)
+
+    async def go():
+        async with McpClient(srv) as c:
+            r = await c.call_tool("get_init_state", {})
+            kinds = [b.type for b in r.content]
+            img = next(b for b in r.content if b.type == "image")
+            ex = McpExecutor({"sokoban": c})
+            rep = await ex.call_tool("sokoban.move_sequence", json.dumps({"directions": ["up"]}))
+            return kinds, img, rep
+    kinds, img, rep = asyncio.run(go())
+    assert kinds == ["text", "image", "text"]
+    assert img.mimeType == "image/jpeg"
+    frame = PILImage.open(io.BytesIO(base64.b64decode(img.data)))
+    assert frame.size == (int(7 * SK.TILE * SK.UPSCALE), int(7 * SK.TILE * SK.UPSCALE))
+    # the fenced metadata block becomes the step's structured output
+    assert rep.structured_output["step_count"] == 1
+    assert rep.structured_output["move_history"] == ["up"]
+    assert "is_passed" in rep.structured_output
