@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--grad-reduce", choices=["push", "nccl"], default="nccl",
                     help="data-parallel gradient reduce-scatter: one NCCL reduce-scatter after "
                          "the backward (default) or copy-engine pushes overlapped with it")
+    ap.add_argument("--dequant-dtype", choices=["bf16", "fp8"], default="bf16",
+                    help="operand type of the expert GEMMs (fp8: e4m3 experts and activations)")
     ap.add_argument("--attention-cache-gb", type=float, default=12.0,
                     help="GB of full-attention outputs kept for the checkpoint recompute")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode window")
@@ -282,7 +284,8 @@ def run_train(args, world: int, rank: int, device):
         max_capacity=args.tokens, pad_to_multiple_of_training=1024, random_init_seed=0,
         use_routing_replay=True, gradient_checkpointing=True, lr_warmup_steps=0,
         learning_rate=1e-5, shard_optimizer_state=not args.replicate_optimizer,
-        attention_cache_gb=args.attention_cache_gb, grad_reduce=args.grad_reduce)
+        attention_cache_gb=args.attention_cache_gb, grad_reduce=args.grad_reduce,
+        dequant_dtype=args.dequant_dtype)
     BenchTrainer = bench_trainer_class()
     from agent_factory_3_b200.trainer.model_trainer import build_model
     t_init = time.perf_counter()
@@ -546,7 +549,7 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "bf16" if args.dequant_dtype == "bf16" else "bf16 (expert GEMMs e4m3)",
             "data": "synthetic (random token ids, random-init weights, MXFP4 experts)",
             "impl": "ours",
             "config": {"model": args.model, "global_batch": int(total_tokens),
