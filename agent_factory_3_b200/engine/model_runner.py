@@ -21,7 +21,7 @@ from ..ops import decode as D
 from ..ops._ext import ext, use_cuda_kernels
 from ..ops.attention import attention_reference
 from ..ops.gemm import matmul
-from ..ops.linear import block_diag_b, lora_linear
+from ..ops.linear import block_diag_b, lora_linear, lora_linear_masked
 from ..ops.norm import rmsnorm
 from ..ops.rope import apply_rope_
 from .kv_cache import PagedKVCache
@@ -34,6 +34,7 @@ class StepItem:
     pages: list[int]        # pages covering start + len(ids) tokens
     want_logits: bool = True
     all_logits: bool = False   # logits of every new token (speculative verify), not just the last
+    adapter: str | None = None  # LoRA adapter of this sequence (mixed-adapter batches)
 
 
 @dataclass
@@ -53,6 +54,7 @@ class ModelRunner:
         self.lora_active = lora_active
         self.device = model.embed_tokens.device
         self._bd_cache: dict = {}
+        self._multi_cache: dict = {}
         self.graphs = None      # engine.cuda_graph.DecodeGraphs when decode steps are captured
 
     def _qkv_lora(self, attn):
@@ -126,7 +128,7 @@ class ModelRunner:
         return m
 
     def _attention(self, li: int, m: "_Meta", xn, qkv_w, qkv_b, A, B, lora_s, sinks, window,
-                   hq: int, hkv: int, pos_cos_sin) -> torch.Tensor:
+                   hq: int, hkv: int, pos_cos_sin, qkv_mask=None) -> torch.Tensor:
         """qkv projection, RoPE, KV store and attention of layer ``li`` for ``hq`` query and
         ``hkv`` KV heads (all heads, or one tensor-parallel rank's slice).  Returns [N, hq*d]."""
         d = self.cfg.head_dim
@@ -134,7 +136,10 @@ class ModelRunner:
         cos, sin = pos_cos_sin
         dev = self.device
         scale = 1.0 / math.sqrt(d)
-        qkv = lora_linear(xn, qkv_w, qkv_b, A, B, None, lora_s)
+        if qkv_mask is not None and A is not None:
+            qkv = lora_linear_masked(xn, qkv_w, qkv_b, A, B, None, lora_s, qkv_mask)
+        else:
+            qkv = lora_linear(xn, qkv_w, qkv_b, A, B, None, lora_s)
         apply_rope_(qkv, hq + hkv, d, m.pos_t, cos, sin)
         kp, vp = self.kv.k[li], self.kv.v[li]
         D.kv_store(qkv, qs, qs + kvs, m.slots_t, kp, vp)
@@ -209,6 +214,126 @@ class ModelRunner:
                                 cfg.swiglu_limit, lay_rec)
             rec.append(lay_rec[0])
         return x, rec
+
+    # ------------------------------------------------------------ mixed-adapter batches
+    def _multi_tensors(self, names: tuple, bank: dict) -> list:
+        """Per layer: the adapters' LoRA factors stacked along the rank, in ``names`` order
+        (cached per adapter set).  bank[name] holds the adapter's factors in the model's own
+        layout (``GptOssForCausalLM.lora_param_dict`` names)."""
+        key = (names, tuple(id(bank[n]) for n in names))
+        hit = self._multi_cache.get("key")
+        if hit is not None and hit[0] == key:
+            return hit[1]
+        cfg = self.cfg
+        dev = self.device
+        bf = torch.bfloat16
+        layers = []
+        for li, layer in enumerate(self.model.layers):
+            a, mlp = layer.self_attn, layer.mlp
+
+            def get(kind, n, name, like):
+                t = bank[n].get(f"layers.{li}.{kind}.{name}")
+                return (t if t is not None else torch.zeros_like(like)).to(dev, bf)
+            ent = {}
+            alist = a.lora
+            if any(k.endswith("_A") and not k.startswith("o_") for k in alist.keys()):
+                As, Bs = [], []
+                r = next(p for k, p in alist.items() if k.endswith("_A")).shape[0]
+                sizes = {"q_proj": cfg.q_size, "k_proj": cfg.kv_size, "v_proj": cfg.kv_size}
+                for n in names:
+                    pa, pb = [], []
+                    for br, out in sizes.items():
+                        za = torch.zeros(r, cfg.hidden_size, device=dev)
+                        zb = torch.zeros(out, r, device=dev)
+                        pa.append(get("self_attn", n, f"{br}_A", za) if f"{br}_A" in alist else za.to(bf))
+                        pb.append(get("self_attn", n, f"{br}_B", zb) if f"{br}_B" in alist else zb.to(bf))
+                    As.append(torch.cat(pa, 0))
+                    Bs.append(block_diag_b(pb))
+                ent["qkv"] = (torch.cat(As, 0).contiguous(), torch.cat(Bs, 1).contiguous(), As[0].shape[0])
+            if "o_proj_A" in alist:
+                oa = [get("self_attn", n, "o_proj_A", alist["o_proj_A"]) for n in names]
+                ob = [get("self_attn", n, "o_proj_B", alist["o_proj_B"]) for n in names]
+                ent["o"] = (torch.cat(oa, 0).contiguous(), torch.cat(ob, 1).contiguous(), oa[0].shape[0])
+            el = {}
+            for k, dim in (("gu_A", 1), ("gu_B", 2), ("dn_A", 1), ("dn_B", 2)):
+                if k in mlp.lora:
+                    el[k] = torch.cat([get("mlp", n, k, mlp.lora[k]) for n in names], dim).contiguous()
+            if el:
+                ent["experts"] = (el, mlp.lora["gu_A"].shape[1] if "gu_A" in mlp.lora
+                                  else mlp.lora["dn_A"].shape[1])
+            layers.append(ent)
+        self._multi_cache["key"] = (key, layers)
+        return layers
+
+    @staticmethod
+    def _rank_mask(row_adapter: torch.Tensor, block: int, n: int) -> torch.Tensor:
+        """[N, n*block] bf16: ones on the rank columns of each row's adapter (row_adapter -1:
+        no adapter, all zeros)."""
+        col = torch.arange(n * block, device=row_adapter.device) // block
+        return (col[None, :] == row_adapter[:, None]).to(torch.bfloat16)
+
+    def _layers_multi(self, m: "_Meta", x: torch.Tensor, row_adapter: torch.Tensor,
+                      tensors: list, n: int) -> tuple[torch.Tensor, list]:
+        from ..ops.moe_layer import moe_forward
+        cfg = self.cfg
+        rope = self.model.rope(self.device)
+        rec: list = []
+        masks: dict = {}
+
+        def mask(block):
+            if block not in masks:
+                masks[block] = self._rank_mask(row_adapter, block, n)
+            return masks[block]
+        for li, layer in enumerate(self.model.layers):
+            a, mlp = layer.self_attn, layer.mlp
+            ent = tensors[li]
+            xn = rmsnorm(x, layer.input_layernorm, cfg.rms_norm_eps)
+            if "qkv" in ent:
+                A, B, blk = ent["qkv"]
+                o = self._attention(li, m, xn, a.qkv_weight, a.qkv_bias, A, B, a.lora_scaling,
+                                    a.sinks, a.window, cfg.num_attention_heads,
+                                    cfg.num_key_value_heads, rope, qkv_mask=mask(blk))
+            else:
+                o = self._attention(li, m, xn, a.qkv_weight, a.qkv_bias, None, None, 1.0,
+                                    a.sinks, a.window, cfg.num_attention_heads,
+                                    cfg.num_key_value_heads, rope)
+            if "o" in ent:
+                oA, oB, blk = ent["o"]
+                h = lora_linear_masked(o, a.o_weight, a.o_bias, oA, oB, x, a.lora_scaling, mask(blk))
+            else:
+                h = lora_linear(o, a.o_weight, a.o_bias, None, None, x, 1.0)
+            hn = rmsnorm(h, layer.post_attention_layernorm, cfg.rms_norm_eps)
+            lay_rec: list = []
+            if "experts" in ent:
+                el, blk = ent["experts"]
+                x = moe_forward(hn, h, mlp.router_weight, mlp.router_bias, mlp.experts(),
+                                cfg.num_experts_per_tok, el, mlp.lora_scaling, None,
+                                cfg.swiglu_alpha, cfg.swiglu_limit, lay_rec,
+                                lora_row_mask=mask(blk))
+            else:
+                x = moe_forward(hn, h, mlp.router_weight, mlp.router_bias, mlp.experts(),
+                                cfg.num_experts_per_tok, None, 1.0, None, cfg.swiglu_alpha,
+                                cfg.swiglu_limit, lay_rec)
+            rec.append(lay_rec[0])
+        return x, rec
+
+    @torch.inference_mode()
+    def forward_mixed(self, items: list[StepItem], bank: dict) -> StepOutput:
+        """One step over sequences that use different adapters (or none): every adapter's
+        LoRA factors are stacked along the rank and each row keeps its own adapter's columns,
+        so the base projections, attention and experts run once for the whole batch."""
+        names = tuple(sorted({it.adapter for it in items if it.adapter is not None}))
+        tensors = self._multi_tensors(names, bank)
+        m = self._meta(items)
+        idx = {n: i for i, n in enumerate(names)}
+        row_adapter = torch.full((m.N,), -1, dtype=torch.long)
+        for (r0, r1), it in zip(m.rows, items):
+            if it.adapter is not None:
+                row_adapter[r0:r1] = idx[it.adapter]
+        row_adapter = row_adapter.to(self.device)
+        x = torch.nn.functional.embedding(m.ids_t, self.model.embed_tokens)
+        x, rec = self._layers_multi(m, x, row_adapter, tensors, len(names))
+        return self._finish(m, items, x, rec)
 
     @torch.inference_mode()
     def forward(self, items: list[StepItem]) -> StepOutput:

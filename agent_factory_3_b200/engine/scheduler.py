@@ -101,6 +101,10 @@ class Engine:
                 from .cuda_graph import DecodeGraphs
                 self.runner.graphs = DecodeGraphs(self.runner)
         self.tp = tp
+        # one GPU: requests of different adapters share a batch (ModelRunner.forward_mixed);
+        # tensor parallel keeps one applied adapter per batch
+        self.mixed_lora = tp is None
+        self.lora_bank: dict = {}
         self.drafter = drafter          # engine.spec drafter: speculative decoding when set
         self.spec_verifies = 0
         self.spec_accepted = 0
@@ -191,9 +195,11 @@ class Engine:
         elif cmd == "load_lora":
             name, path = args
             self.loras[name] = self._read_adapter(path)
+            self.lora_bank.pop(name, None)
             return True
         elif cmd == "unload_lora":
             self.loras.pop(args[0], None)
+            self.lora_bank.pop(args[0], None)
             if self.active_lora == args[0]:
                 self.active_lora = None
                 self.runner.lora_active = False
@@ -205,11 +211,13 @@ class Engine:
         elif cmd == "apply_lora_params":    # staged tensors in the model's own LoRA layout
             name, sd = args
             self.loras[name] = ("params", sd)
+            self.lora_bank.pop(name, None)
             self._apply_lora(name)
             return True
         elif cmd == "set_lora_tensors":     # in-memory adapter (direct weight sync)
             name, sd = args
             self.loras[name] = sd
+            self.lora_bank.pop(name, None)
             if self.active_lora == name:
                 self._apply_lora(name)
         return None
@@ -221,6 +229,29 @@ class Engine:
             return torch.load(p / "adapter_model.bin", map_location="cpu", weights_only=True)
         from safetensors.torch import load_file
         return load_file(str(p / "adapter_model.safetensors"))
+
+    def _bank(self, name: str) -> dict:
+        """Adapter ``name``'s factors in the model's own layout (bf16 on the device), for
+        mixed-adapter steps; built once per adapter version.  A PEFT state dict is converted by
+        loading it into the model's LoRA parameters and restoring the applied adapter after."""
+        hit = self.lora_bank.get(name)
+        if hit is not None:
+            return hit
+        ad = self.loras[name]
+        dev = self.model.embed_tokens.device
+        if isinstance(ad, tuple) and ad[0] == "params":
+            params = self.model.lora_param_dict()
+            bank = {k: t.to(dev, torch.bfloat16).view(params[k].shape) for k, t in ad[1].items()}
+        else:
+            params = self.model.lora_param_dict()
+            saved = {k: p.detach().clone() for k, p in params.items()}
+            _load_lora_into(self.model, ad)
+            bank = {k: p.detach().to(torch.bfloat16).clone() for k, p in params.items()}
+            with torch.no_grad():
+                for k, p in params.items():
+                    p.copy_(saved[k])
+        self.lora_bank[name] = bank
+        return bank
 
     def _apply_lora(self, name: str) -> None:
         ad = self.loras[name]
@@ -297,8 +328,14 @@ class Engine:
         P = self.kv.page_size
         while self.waiting and len(self.running) < self.max_running:
             r = self.waiting[0]
-            if r.lora_path != self.active_lora:
-                if self.running:       # adapters switch only between batches
+            if self.mixed_lora:
+                # one GPU: sequences of different adapters share a batch (stacked-rank LoRA)
+                if r.lora_path is not None and r.lora_path not in self.loras:
+                    self.waiting.popleft()
+                    self._finish(r, {"type": "abort", "message": f"unknown lora {r.lora_path}"})
+                    continue
+            elif r.lora_path != self.active_lora:
+                if self.running:       # tensor parallel: adapters switch only between batches
                     break
                 if r.lora_path is None:
                     self.active_lora = None
@@ -394,18 +431,20 @@ class Engine:
             except OutOfPages:
                 continue
             items.append(StepItem(ids=ids[r.n_cached:r.n_cached + n], start=r.n_cached,
-                                  pages=list(r.pages), want_logits=(r.n_cached + n == len(ids))))
+                                  pages=list(r.pages), want_logits=(r.n_cached + n == len(ids)),
+                                  adapter=r.lora_path))
             owners.append(r)
         n_plain = len(items)
         if spec_reqs:
             drafts = self.drafter.propose([r.all_ids for r in spec_reqs], spec_sizes)
             for r, d in zip(spec_reqs, drafts):
                 items.append(StepItem(ids=[r.all_ids[-1]] + list(d), start=r.n_cached,
-                                      pages=list(r.pages), want_logits=True, all_logits=True))
+                                      pages=list(r.pages), want_logits=True, all_logits=True,
+                                      adapter=r.lora_path))
                 owners.append(r)
         if not items:
             return
-        out = self.runner.forward(items)
+        out = self._forward(items)
         self.step_count += 1
         plain = [i for i in range(n_plain) if items[i].want_logits]
         sample_owners = [owners[i] for i in plain]
@@ -466,6 +505,19 @@ class Engine:
             else:
                 still.append(r)
         self.running = still
+
+    def _forward(self, items: list[StepItem]):
+        if not self.mixed_lora:
+            return self.runner.forward(items)
+        adapters = {it.adapter for it in items}
+        if len(adapters) > 1:
+            return self.runner.forward_mixed(items, {n: self._bank(n) for n in adapters if n})
+        (name,) = adapters
+        if name is None:
+            self.runner.lora_active = False
+        elif name != self.active_lora or not self.runner.lora_active:
+            self._apply_lora(name)
+        return self.runner.forward(items)
 
     # ------------------------------------------------------------------ outputs
     def _meta(self, r: Request, final: bool) -> dict:

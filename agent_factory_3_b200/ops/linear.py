@@ -75,5 +75,16 @@ class LoraLinearFn(torch.autograd.Function):
         return dx, None, None, dA, dB, dres, None
 
 
+@torch.no_grad()
+def lora_linear_masked(x, W, bias, A, B, residual, s, row_mask):
+    """Inference form for batches that mix adapters: the adapters' factors are stacked along
+    the rank (A [sum R_a, in], B [out, sum R_a]) and ``row_mask`` [T, sum R_a] (0/1, bf16) keeps
+    each row's own adapter's rank columns, so one dual GEMM applies a different adapter per row:
+    y = x W^T + b + ((s x A^T) * mask) B^T (+ residual).  A row whose columns are all zero gets
+    the base projection only."""
+    xa = G.matmul(x, _bf16(A), alpha=s) * row_mask
+    return G.matmul(x, W, bias=bias, residual=residual, a2=xa, b2=_bf16(B))
+
+
 def lora_linear(x, W, bias=None, A=None, B=None, residual=None, s=1.0):
     return LoraLinearFn.apply(x, W, bias, A, B, residual, s)

@@ -132,6 +132,13 @@ def _b(t):
     return None if t is None else t.to(torch.bfloat16)
 
 
+def _sorted_mask(row_mask: torch.Tensor, rt) -> torch.Tensor:
+    """Per-token LoRA rank mask [T, R] -> per expert-sorted row (padding rows zero)."""
+    src = rt.row_src.long()
+    m = row_mask.index_select(0, src.clamp(min=0))
+    return m * (src >= 0).to(m.dtype)[:, None]
+
+
 def mxfp4_int_cvt(experts: ExpertWeights) -> int:
     """1 to run the MXFP4-direct kernel's integer e2m1 -> f16 conversion (AF3_MXFP4_CVT=int and
     every scale byte <= 128).  The default is the hardware conversion instruction, measured
@@ -144,7 +151,7 @@ def mxfp4_int_cvt(experts: ExpertWeights) -> int:
 class MoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, xn, residual, router_w, router_b, gu_A, gu_B, dn_A, dn_B, experts,
-                top_k, replay_ids, s, act_alpha, act_limit, routing_out):
+                top_k, replay_ids, s, act_alpha, act_limit, routing_out, lora_row_mask=None):
         T, H = xn.shape
         E = router_w.shape[0]
         logits = G.matmul(xn, router_w, bias=router_b, out_dtype=torch.float32)
@@ -160,12 +167,17 @@ class MoEFn(torch.autograd.Function):
                                       top_k, s, act_alpha, act_limit, need_grad)
         W_gu = experts.gate_up()
         xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if lora_gu else None
+        sm = _sorted_mask(lora_row_mask, rt) if lora_row_mask is not None else None
+        if sm is not None and xa is not None:
+            xa = xa * sm
         h, gu = G.grouped_matmul(x_s, W_gu, rt.offsets, epilogue="swiglu", bias=experts.gu_bias,
                                  act_alpha=act_alpha, act_limit=act_limit,
                                  save_preact=need_grad, a2=xa,
                                  b2=_b(gu_B) if lora_gu else None)
         W_dn = experts.down()
         ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if lora_dn else None
+        if sm is not None and ha is not None:
+            ha = ha * sm
         y_s, _ = G.grouped_matmul(h, W_dn, rt.offsets, epilogue="rowscale", bias=experts.dn_bias,
                                   row_scale=rt.row_gate, a2=ha,
                                   b2=_b(dn_B) if lora_dn else None)
@@ -258,7 +270,7 @@ class MoEFn(torch.autograd.Function):
             dx_s, _ = fp8.grouped_matmul_f8(d_q, d_sc, W_guT, s_gu, rt.offsets)
         dxn = M.combine_rows(dx_s, rt.dest, top_k)
         return (dxn, dout, None, None, d_guA, d_guB, d_dnA, d_dnB, None, None, None, None, None,
-                None, None)
+                None, None, None)
 
     @staticmethod
     def backward(ctx, dout):
@@ -295,7 +307,7 @@ class MoEFn(torch.autograd.Function):
             dx_s, _ = G.grouped_matmul(dgu, W_gu, rt.offsets, b_layout="kn")
         dxn = M.combine_rows(dx_s, rt.dest, top_k)
         return (dxn, dout, None, None, d_guA, d_guB, d_dnA, d_dnB, None, None, None, None, None,
-                None, None)
+                None, None, None)
 
 
 def _mxfp4_direct(xn: torch.Tensor, experts: ExpertWeights, E: int, top_k: int) -> bool:
@@ -320,7 +332,7 @@ def _token_tile(rows: int, E: int) -> int:
 def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, top_k: int,
                       lora: dict | None = None, s: float = 1.0, replay_ids=None,
                       act_alpha: float = 1.702, act_limit: float = 7.0,
-                      routing_out: list | None = None):
+                      routing_out: list | None = None, lora_row_mask=None):
     """Inference MoE that reads the MXFP4 expert weights directly (no bf16 copy): the
     swap-AB kernel tiles 128 weight rows x the few tokens of each expert, and expert LoRA
     (x A_e^T s) B_e^T joins the same accumulation as extra K blocks."""
@@ -337,12 +349,17 @@ def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, 
     I2 = experts.gu_blocks.shape[1]
     gu_A, gu_B, dn_A, dn_B = (lora.get(k) for k in ("gu_A", "gu_B", "dn_A", "dn_B"))
     xa = G.grouped_matmul(x_s, _b(gu_A), rt.offsets, alpha=s)[0] if gu_A is not None else None
+    sm = _sorted_mask(lora_row_mask, rt) if lora_row_mask is not None else None
+    if sm is not None and xa is not None:
+        xa = xa * sm
     h = torch.empty(R, I2 // 2, device=xn.device, dtype=torch.bfloat16)
     ic = mxfp4_int_cvt(experts)
     ext().moe_mxfp4_gemm(x_s, experts.gu_blocks, experts.gu_scales, experts.gu_bias, rt.offsets,
                          rt.counts, 0, None, h, act_alpha, act_limit, bn,
                          lora_b=_b(gu_B) if xa is not None else None, xa=xa, int_cvt=ic)
     ha = G.grouped_matmul(h, _b(dn_A), rt.offsets, alpha=s)[0] if dn_A is not None else None
+    if sm is not None and ha is not None:
+        ha = ha * sm
     y_s = torch.empty(R, H, device=xn.device, dtype=torch.bfloat16)
     ext().moe_mxfp4_gemm(h, experts.dn_blocks, experts.dn_scales, experts.dn_bias, rt.offsets,
                          rt.counts, 1, rt.row_gate, y_s, act_alpha, act_limit, bn,
@@ -352,11 +369,15 @@ def moe_forward_mxfp4(xn, residual, router_w, router_b, experts: ExpertWeights, 
 
 def moe_forward(xn, residual, router_w, router_b, experts: ExpertWeights, top_k: int,
                 lora: dict | None = None, s: float = 1.0, replay_ids=None,
-                act_alpha: float = 1.702, act_limit: float = 7.0, routing_out: list | None = None):
+                act_alpha: float = 1.702, act_limit: float = 7.0, routing_out: list | None = None,
+                lora_row_mask: torch.Tensor | None = None):
+    """``lora_row_mask`` [T, R] (0/1): per-token selection of expert-LoRA rank columns when
+    ``lora`` holds several adapters stacked along the rank (mixed-adapter inference batches);
+    the gate_up and down factors must use the same column layout."""
     lora = lora or {}
     if _mxfp4_direct(xn, experts, router_w.shape[0], top_k):
         return moe_forward_mxfp4(xn, residual, router_w, router_b, experts, top_k, lora, s,
-                                 replay_ids, act_alpha, act_limit, routing_out)
+                                 replay_ids, act_alpha, act_limit, routing_out, lora_row_mask)
     return MoEFn.apply(xn, residual, router_w, router_b, lora.get("gu_A"), lora.get("gu_B"),
                        lora.get("dn_A"), lora.get("dn_B"), experts, top_k, replay_ids, s,
-                       act_alpha, act_limit, routing_out)
+                       act_alpha, act_limit, routing_out, lora_row_mask)

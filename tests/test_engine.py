@@ -213,3 +213,75 @@ def test_top_logprobs_are_the_k_best_tokens():
         want_v, want_i = lp[pos].topk(5)
         assert [e[1] for e in row][:2] == want_i.tolist()[:2] or abs(vals[0] - vals[1]) < 1e-4
         assert abs(vals[0] - float(want_v[0])) < 1e-3
+
+
+def _adapter_params(model, seed):
+    g = torch.Generator().manual_seed(seed)
+    return {k: torch.randn(p.shape, generator=g) * 0.2 for k, p in model.lora_param_dict().items()}
+
+
+def test_mixed_adapter_step_matches_single_adapter_runs():
+    """One step over sequences of adapter A, adapter B and no adapter (stacked-rank LoRA with
+    per-row rank masks) gives each sequence the logits of a step run with only its adapter."""
+    from agent_factory_3_b200.engine.model_runner import ModelRunner, StepItem
+    lora = LoraConfig(r=4, lora_alpha=8, target_modules=["q_proj", "k_proj", "v_proj", "o_proj",
+                                                         "gate_up_proj", "down_proj"])
+    model = tiny_model(lora=lora)
+    cfg = model.cfg
+    bank = {"A": _adapter_params(model, 1), "B": _adapter_params(model, 2)}
+    prompts = {"A": list(range(3, 40)), "B": list(range(50, 71)), None: list(range(80, 93))}
+
+    def kv():
+        return PagedKVCache(cfg.num_hidden_layers, 32, 16, cfg.num_key_value_heads, cfg.head_dim,
+                            cfg.num_experts_per_tok, "cpu", torch.float32)
+    pages = {"A": [0, 1, 2], "B": [3, 4], None: [5]}
+    runner = ModelRunner(model, kv(), lora_active=True)
+    items = [StepItem(prompts[a], 0, pages[a], adapter=a) for a in ("A", "B", None)]
+    mixed = runner.forward_mixed(items, bank).logits
+    params = model.lora_param_dict()
+    for j, a in enumerate(("A", "B", None)):
+        single = ModelRunner(model, kv(), lora_active=a is not None)
+        if a is not None:
+            with torch.no_grad():
+                for k, p in params.items():
+                    p.copy_(bank[a][k])
+        ref = single.forward([StepItem(prompts[a], 0, pages[a])]).logits[0]
+        torch.testing.assert_close(mixed[j], ref, rtol=1e-4, atol=1e-4)
+
+
+def test_engine_batches_requests_of_different_adapters_together():
+    lora = LoraConfig(r=4, lora_alpha=8, target_modules=["q_proj", "v_proj", "o_proj",
+                                                         "gate_up_proj", "down_proj"])
+    model = tiny_model(lora=lora)
+    eng = Engine(model, num_pages=64, page_size=16)
+    calls = {"mixed": 0}
+    orig = eng.runner.forward_mixed
+
+    def counting(items, bank):
+        calls["mixed"] += 1
+        return orig(items, bank)
+    eng.runner.forward_mixed = counting
+    eng.start()
+    try:
+        eng.control("apply_lora_params", "A", _adapter_params(model, 1))
+        eng.control("apply_lora_params", "B", _adapter_params(model, 2))
+
+        async def run():
+            c = await _client(eng)
+            try:
+                bodies = [{"input_ids": list(range(3 + 7 * i, 20 + 7 * i)),
+                           "sampling_params": {"max_new_tokens": 6, "temperature": 0.0},
+                           **({"lora_path": a} if a else {})}
+                          for i, a in enumerate(("A", "B", None, "A"))]
+                res = await asyncio.gather(*(c.post("/generate", json=b) for b in bodies))
+                outs = [await r.json() for r in res]
+                bad = await c.post("/generate", json=dict(bodies[0], lora_path="missing"))
+                return outs, (await bad.json())
+            finally:
+                await c.close()
+        outs, bad = asyncio.run(run())
+    finally:
+        eng.stop()
+    assert all(len(o["output_ids"]) == 6 for o in outs)
+    assert calls["mixed"] > 0
+    assert bad["meta_info"]["finish_reason"]["type"] == "abort"
