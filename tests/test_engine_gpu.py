@@ -115,3 +115,41 @@ def test_engine_greedy_gpu(dev):
     assert bool((chosen >= lg.max(-1).values - 0.05).all()), (out, lg.argmax(-1).tolist())
     assert b["output_ids"] == a["output_ids"]
     assert b["meta_info"]["cached_tokens"] >= 128
+
+
+def test_mixed_adapter_step_gpu(dev):
+    """Mixed-adapter step on the GPU kernels (masked dual GEMMs, MXFP4-direct experts with
+    masked LoRA K blocks) against single-adapter steps."""
+    from agent_factory_3_b200.engine.kv_cache import PagedKVCache
+    from agent_factory_3_b200.engine.model_runner import ModelRunner, StepItem
+    from agent_factory_3_b200.models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
+    cfg = GptOssConfig(vocab_size=2048, hidden_size=256, intermediate_size=256, num_hidden_layers=2,
+                       num_attention_heads=8, num_key_value_heads=2, head_dim=64,
+                       num_local_experts=8, num_experts_per_tok=2, sliding_window=32,
+                       rope_scaling=None, max_position_embeddings=4096, pad_token_id=0,
+                       eos_token_id=1)
+    lora = LoraConfig(r=16, lora_alpha=32, target_modules=["q_proj", "k_proj", "v_proj", "o_proj",
+                                                           "gate_up_proj", "down_proj"])
+    model = GptOssForCausalLM(cfg, lora=lora, device=dev).init_random(0).eval()
+    params = model.lora_param_dict()
+    bank = {}
+    for name, seed in (("A", 1), ("B", 2)):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        bank[name] = {k: (torch.randn(p.shape, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+                      for k, p in params.items()}
+    prompts = {"A": list(range(3, 140)), "B": list(range(150, 171)), None: list(range(200, 213))}
+    pages = {"A": [0, 1, 2], "B": [3], None: [4]}
+
+    def kv():
+        return PagedKVCache(2, 16, 64, 2, 64, 2, dev, torch.bfloat16)
+    mixed = ModelRunner(model, kv()).forward_mixed(
+        [StepItem(prompts[a], 0, pages[a], adapter=a) for a in ("A", "B", None)], bank).logits
+    for j, a in enumerate(("A", "B", None)):
+        if a is not None:
+            with torch.no_grad():
+                for k, p in params.items():
+                    p.copy_(bank[a][k].float())
+        ref = ModelRunner(model, kv(), lora_active=a is not None).forward(
+            [StepItem(prompts[a], 0, pages[a])]).logits[0]
+        err = (mixed[j] - ref).abs().max().item()
+        assert err <= 0.02 * ref.abs().max().item() + 1e-3, (a, err)
