@@ -54,6 +54,14 @@ struct Params {
   int* err;
 };
 
+// Bounded wait whose result is the same on every lane of the warp (a lane that timed out makes
+// the whole warp give up), so the per-warp arrives after __syncwarp never diverge.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err,
+                                               volatile int* abort_flag) {
+  const bool ok = mbar_wait(bar, parity, err, abort_flag);
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -192,14 +200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&qdo_full[s], 1);
       mbar_init(&qdo_empty[s], 1);
-      mbar_init(&ld_full[s], 32);
-      mbar_init(&ld_empty[s], 256);
+      // consumer-side barriers take one arrive per warp (lane 0 after __syncwarp), not one per
+      // thread: hundreds of per-thread arrives per block serialise on the barrier word
+      mbar_init(&ld_full[s], 1);
+      mbar_init(&ld_empty[s], 8);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
-      mbar_init(&p_full[s], 256);
+      mbar_init(&s_empty[s], 4);
+      mbar_init(&p_full[s], 8);
       mbar_init(&mma_done[s], 1);
       mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_empty[s], 128);
+      mbar_init(&dq_empty[s], 4);
     }
     mbar_init(final_done, 1);
     *abort_flag = 0;
@@ -235,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------- lse / D loader (plain loads) -----------------------------
     for (int it = 0; it < n_it; ++it) {
       const int s = it & 1;
-      if (!mbar_wait(&ld_empty[s], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) break;
+      if (!mbar_wait_warp(&ld_empty[s], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) break;
       const int h = g * rep + it / nqb;
       const int qb = k0 + (it % nqb) * kB;
       float* dst = reinterpret_cast<float*>(smem + Smem::LD + s * 2 * kB * 4);
@@ -245,7 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         dst[c] = ok ? p.lse[(int64_t)h * p.T + qi] * kLog2e : INFINITY;
         dst[kB + c] = ok ? p.Dd[(int64_t)h * p.T + qi] : 0.f;
       }
-      mbar_arrive(&ld_full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ld_full[s]);
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer --------------------------------------
@@ -324,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = qd * 32 + lane;  // query row of the block
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
     for (int j = 0; j < n_it; ++j) {
-      if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
+      if (!mbar_wait_warp(&dq_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
       tc_fence_after();
       const int h = g * rep + j / nqb;
       const int qi = k0 + (j % nqb) * kB + r;
@@ -333,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_32x32b_x32(tmem + lb + 416 + (j & 1) * kHD, v1);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&dq_empty[j & 1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_empty[j & 1]);
       if (qi < q_end) {
         float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
 #pragma unroll
@@ -359,13 +371,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
       // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
-      if (it >= 2 && !mbar_wait(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+      if (it >= 2 && !mbar_wait_warp(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
       const int s = it & 1;
-      if (!mbar_wait(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(&s_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const float* lds = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);  // lse2, D
       const int qb = k0 + (it % nqb) * kB;
@@ -410,13 +422,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           if (q == 2) {   // every S^T / dP^T column of this half is in registers
             tc_fence_before();
-            mbar_arrive(&s_empty[hf]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[hf]);
           }
         }
       }
-      mbar_arrive(&ld_empty[s]);
       fence_proxy_async_smem();
-      mbar_arrive(&p_full[it & 1]);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&ld_empty[s]);
+        mbar_arrive(&p_full[it & 1]);
+      }
     }
     if (ok && mbar_wait(final_done, 0, p.err, abort_flag)) {
       // half 0 writes dV, half 1 writes dK
