@@ -14,9 +14,12 @@
 // warpgroup (warps 4-7: queries 0-63, warps 12-15: queries 64-127) and its own TMEM
 // full/empty barriers: a half's S^T / dP^T of the next block is computed as soon as that
 // warpgroup has read the current one, so the tensor core overlaps the softmax.
-// dQ of each block is added to an fp32 buffer with 16-byte vector atomics by warps 8-11; dK
-// and dV are complete at the end of the CTA (all q heads of the group were visited) and are
-// written once as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the
+// dQ of each block is added to an fp32 buffer by warps 8-11: they stage it, scaled, in the
+// block's P^T buffer (free once the block's MMAs completed, until the softmax of block+2 writes
+// it) as four 32-row x 64-column 128B-swizzled boxes, and each warp issues TMA reduce-adds of
+// its two [32 x 32] boxes, so the L2 adds whole lines; the warp releases the buffer to the
+// softmax once the TMA has read it.  dK and dV are complete at the end of the CTA (all q heads
+// of the group were visited) and are written once as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the
 // sink gradient d(sink_h) = -sum_i exp(sink_h - lse_h(i)) * D_h(i); an epilogue kernel
 // converts dQ to bf16.
 #include "common.h"
@@ -156,7 +159,8 @@ __device__ __forceinline__ void softmax_grad16(const uint32_t (&sv)[16], const u
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tma_qkv,
-                    const __grid_constant__ CUtensorMap tma_do, const Params p) {
+                    const __grid_constant__ CUtensorMap tma_do,
+                    const __grid_constant__ CUtensorMap tma_dq, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // the layout uses all 227 KB, so there is no slack to realign: require a 1024-aligned base
   uint8_t* smem = smem_raw;
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 9;     // [2] per query half
   uint64_t* s_empty = bars + 11;   // [2] per query half
   uint64_t* p_full = bars + 13;    // [2] P^T/dS^T buffer b written
-  uint64_t* mma_done = bars + 15;  // [2] P^T/dS^T buffer b consumed
+  uint64_t* pt_free = bars + 15;   // [2] P^T/dS^T buffer b consumed (MMAs, dQ staging read)
   uint64_t* dq_full = bars + 17;   // [2]
   uint64_t* dq_empty = bars + 19;  // [2]
   uint64_t* final_done = bars + 21;
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_qkv);
     tma_prefetch_desc(&tma_do);
+    tma_prefetch_desc(&tma_dq);
     mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&qdo_full[s], 1);
@@ -207,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
       mbar_init(&p_full[s], 8);
-      mbar_init(&mma_done[s], 1);
+      mbar_init(&pt_free[s], 4);
       mbar_init(&dq_full[s], 1);
       mbar_init(&dq_empty[s], 4);
     }
@@ -322,7 +327,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
             umma_f16(tmem + 384 + (j & 1) * kHD, a, b, id_q, kk > 0);
           }
-          umma_commit(&mma_done[j & 1]);
           umma_commit(&dq_full[j & 1]);
           umma_commit(&qdo_empty[s]);
         }
@@ -330,15 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) umma_commit(final_done);
     }
   } else if (warp >= 8 && warp < 12) {
-    // ------------------------- dQ drain (TMEM -> fp32 atomics) ------------------------
+    // ------------- dQ drain (TMEM -> swizzled smem -> TMA reduce-add into fp32) -------------
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;  // query row of the block
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
     for (int j = 0; j < n_it; ++j) {
       if (!mbar_wait_warp(&dq_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
       tc_fence_after();
       const int h = g * rep + j / nqb;
-      const int qi = k0 + (j % nqb) * kB + r;
+      const int q0 = k0 + (j % nqb) * kB + qd * 32;  // first query row of this warp
       uint32_t v0[32], v1[32];
       tmem_ld_32x32b_x32(tmem + lb + 384 + (j & 1) * kHD, v0);
       tmem_ld_32x32b_x32(tmem + lb + 416 + (j & 1) * kHD, v1);
@@ -346,21 +349,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_empty[j & 1]);
-      if (qi < q_end) {
-        float4* dst = reinterpret_cast<float4*>(p.dq + (int64_t)qi * (p.hq * kHD) + h * kHD);
+      // rows past q_end hold exact zeros (their P is masked), so only whole-warp tails skip
+      if (q0 < q_end) {
+        // the MMAs of block j completed, so its P^T buffer is free until block j+2
+        uint8_t* stage = smem + Smem::PT + (j & 1) * kB * kB * 2 + qd * 8192;
+        const uint32_t sw = smem_u32(stage) + lane * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          atomicAdd(dst + c, make_float4(__uint_as_float(v0[4 * c]) * p.scale,
-                                         __uint_as_float(v0[4 * c + 1]) * p.scale,
-                                         __uint_as_float(v0[4 * c + 2]) * p.scale,
-                                         __uint_as_float(v0[4 * c + 3]) * p.scale));
-          atomicAdd(dst + 8 + c, make_float4(__uint_as_float(v1[4 * c]) * p.scale,
-                                             __uint_as_float(v1[4 * c + 1]) * p.scale,
-                                             __uint_as_float(v1[4 * c + 2]) * p.scale,
-                                             __uint_as_float(v1[4 * c + 3]) * p.scale));
+          const uint32_t o = ((c ^ (lane & 7)) * 16);
+          st_shared_v4(sw + o, __float_as_uint(__uint_as_float(v0[4 * c]) * p.scale),
+                       __float_as_uint(__uint_as_float(v0[4 * c + 1]) * p.scale),
+                       __float_as_uint(__uint_as_float(v0[4 * c + 2]) * p.scale),
+                       __float_as_uint(__uint_as_float(v0[4 * c + 3]) * p.scale));
+          st_shared_v4(sw + 4096 + o, __float_as_uint(__uint_as_float(v1[4 * c]) * p.scale),
+                       __float_as_uint(__uint_as_float(v1[4 * c + 1]) * p.scale),
+                       __float_as_uint(__uint_as_float(v1[4 * c + 2]) * p.scale),
+                       __float_as_uint(__uint_as_float(v1[4 * c + 3]) * p.scale));
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tma_dq, stage, h * kHD, q0);
+          tma_reduce_add_2d(&tma_dq, stage + 4096, h * kHD + 32, q0);
+          bulk_commit();
+          bulk_wait_read();
+        }
+        __syncwarp();
       }
+      if (lane == 0) mbar_arrive(&pt_free[j & 1]);
     }
+    if (lane == 0) bulk_wait_all();
   } else if (warp >= 4) {
     // ---------------- softmax gradient (P^T, dS^T) of one half of the queries ----------
     const int hf = warp >= 12 ? 1 : 0;
@@ -370,8 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key = k0 + r;
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
-      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
-      if (it >= 2 && !mbar_wait_warp(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed and the
+      // dQ staging of that block has been read by the TMA
+      if (it >= 2 && !mbar_wait_warp(&pt_free[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -544,6 +563,12 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
   const uint64_t dstrides[1] = {(uint64_t)dout.stride(0) * 2};
   CUtensorMap tdo = make_tmap(dout.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ddims,
                               dstrides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  // dQ accumulator: fp32 [T, hq*64]; boxes of 32 rows x 32 columns (128 B, the swizzle span)
+  const uint64_t qdims[2] = {(uint64_t)(hq * kHD), (uint64_t)T};
+  const uint64_t qstrides[1] = {(uint64_t)(hq * kHD * 4)};
+  const uint32_t qbox[2] = {32, 32};
+  CUtensorMap tdq = make_tmap(dq.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, qdims, qstrides,
+                              qbox, CU_TENSOR_MAP_SWIZZLE_128B);
   Params p;
   p.tiles = kv_tiles.data_ptr<int>();
   p.lse = lse.data_ptr<float>();
@@ -568,7 +593,7 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
     attr[dev] = true;
   }
   dim3 grid((unsigned)hkv, (unsigned)n_tiles);
-  attn_bwd_kernel<<<grid, kThreads, smem, stream>>>(tq, tdo, p);
+  attn_bwd_kernel<<<grid, kThreads, smem, stream>>>(tq, tdo, tdq, p);
   AF3_CUDA_CHECK(cudaGetLastError());
   const int64_t n4 = T * hq * kHD / 4;
   attn_bwd_post_kernel<<<std::min<int64_t>((n4 + 255) / 256, num_sms() * 16), 256, 0, stream>>>(

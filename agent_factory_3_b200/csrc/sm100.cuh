@@ -176,6 +176,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Element-wise add of a 2-D shared-memory box into global memory through the tensor map (the
+// L2 performs the adds on whole lines).  Completion is tracked by the issuing thread's bulk
+// groups: commit with bulk_commit(), then bulk_wait_read() before the shared memory is reused.
+// Coordinates must be non-negative; rows or columns past the tensor's extent are dropped.
+__device__ __forceinline__ void tma_reduce_add_2d(const void* desc, const void* src, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The shared-memory sources of every committed bulk group have been read.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every committed bulk group has completed (its global writes are done).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Order generic-proxy shared-memory writes before async-proxy (tensor core / TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
