@@ -5,11 +5,15 @@
 // loops over every q head of the kv group and every 128-query block that can see the tile:
 //   S^T  = K Q^T        (tcgen05, M=128 keys, N=64 queries per half, K=64)  TMEM cols   0..127
 //   dP^T = V dO^T       (same shape)                                        TMEM cols 128..255
+//          K and V are the A operands of these two products and are read from TMEM (cols
+//          448..479 and 480..511, copied there once per CTA): with N = 64, an MMA that reads
+//          both operands from shared memory is bound by shared-memory bandwidth, and shared
+//          memory is the busiest unit of this kernel.
 //   P^T  = 2^(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - D[q])   (softmax warps,
 //          thread = key row, written as bf16 into 128B-swizzled shared memory)
 //   dV  += P^T dO       (A = P^T K-major, B = dO as MN-major)         TMEM cols 256..319
 //   dK  += dS^T Q       (A = dS^T, B = Q as MN-major)                 TMEM cols 320..383
-//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..511 (x2)
+//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..447
 // The 128 query columns of S^T / dP^T are split into two halves, each with its own softmax
 // warpgroup (warps 4-7: queries 0-63, warps 12-15: queries 64-127) and its own TMEM
 // full/empty barriers: a half's S^T / dP^T of the next block is computed as soon as that
@@ -33,6 +37,9 @@ constexpr int kThreads = 512;
 constexpr int kHD = 64;
 constexpr int kB = 128;  // keys per CTA tile, queries per block
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kColDQ = 384;  // dQ accumulator (64 columns, one block at a time)
+constexpr int kColK = 448;   // K as bf16 pairs: the A operand of S^T
+constexpr int kColV = 480;   // V as bf16 pairs: the A operand of dP^T
 
 struct Smem {
   static constexpr int K = 0;                         // 16 KB  [128 keys x 64] K-major
@@ -181,7 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_full = bars + 17;   // [2]
   uint64_t* dq_empty = bars + 19;  // [2]
   uint64_t* final_done = bars + 21;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* kv_tmem = bars + 22;   // K and V copied into TMEM
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -213,10 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_empty[s], 4);
       mbar_init(&p_full[s], 8);
       mbar_init(&pt_free[s], 4);
-      mbar_init(&dq_full[s], 1);
-      mbar_init(&dq_empty[s], 4);
+      mbar_init(&dq_full[s], 1);   // only [0] is used
+      mbar_init(&dq_empty[s], 4);  // only [0] is used: one dQ accumulator
     }
     mbar_init(final_done, 1);
+    mbar_init(kv_tmem, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -269,9 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_s = make_idesc_bf16(kB, kB / 2, false, false);  // S^T, dP^T halves
       constexpr uint32_t id_kv = make_idesc_bf16(kB, kHD, false, true);     // dV, dK
       constexpr uint32_t id_q = make_idesc_bf16(kB, kHD, true, true);       // dQ
-      const uint32_t sK = smem_u32(smem + Smem::K), sV = smem_u32(smem + Smem::V);
+      const uint32_t sK = smem_u32(smem + Smem::K);
       const uint32_t sPT = smem_u32(smem + Smem::PT), sDS = smem_u32(smem + Smem::DST);
-      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag);
+      bool ok = mbar_wait(kv_tmem, 0, p.err, abort_flag);
+      tc_fence_after();
       for (int it = 0; ok && it <= n_it; ++it) {
         if (it < n_it) {
           const int s = it & 1;
@@ -284,15 +294,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             // queries hf*64 .. hf*64+63 start 64 rows (8 KB, swizzle-atom aligned) in
 #pragma unroll
             for (int kk = 0; kk < kHD / 16; ++kk) {
-              umma_f16(tmem + hf * 64, make_smem_desc(sK + kk * 32, 16, 1024, kLayoutSW128),
-                       make_smem_desc(sQ + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128), id_s,
-                       kk > 0);
+              umma_f16_tmem_a(tmem + hf * 64, tmem + kColK + kk * 8,
+                              make_smem_desc(sQ + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
+                              id_s, kk > 0);
             }
 #pragma unroll
             for (int kk = 0; kk < kHD / 16; ++kk) {
-              umma_f16(tmem + 128 + hf * 64, make_smem_desc(sV + kk * 32, 16, 1024, kLayoutSW128),
-                       make_smem_desc(sDO + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128), id_s,
-                       kk > 0);
+              umma_f16_tmem_a(tmem + 128 + hf * 64, tmem + kColV + kk * 8,
+                              make_smem_desc(sDO + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
+                              id_s, kk > 0);
             }
             umma_commit(&s_full[hf]);
           }
@@ -302,7 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int j = it - 1;
           const int s = j & 1;
           if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
-          if (!mbar_wait(&dq_empty[j & 1], ((j >> 1) & 1) ^ 1, p.err, abort_flag)) break;
+          // the drain has read the previous block's dQ out of TMEM
+          if (!mbar_wait(&dq_empty[0], (j & 1) ^ 1, p.err, abort_flag)) break;
           tc_fence_after();
           const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
           const uint32_t sDO = sQ + kB * kHD * 2;
@@ -325,9 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // reduction over the 128 keys: A = dS (M = queries) read from dS^T as MN-major
             const uint64_t a = make_smem_desc(sDSb + kk * 2048, 16384, 1024, kLayoutSW128);
             const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
-            umma_f16(tmem + 384 + (j & 1) * kHD, a, b, id_q, kk > 0);
+            umma_f16(tmem + kColDQ, a, b, id_q, kk > 0);
           }
-          umma_commit(&dq_full[j & 1]);
+          umma_commit(&dq_full[0]);
           umma_commit(&qdo_empty[s]);
         }
       }
@@ -338,17 +349,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qd = warp & 3;
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
     for (int j = 0; j < n_it; ++j) {
-      if (!mbar_wait_warp(&dq_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
+      if (!mbar_wait_warp(&dq_full[0], j & 1, p.err, abort_flag)) break;
       tc_fence_after();
       const int h = g * rep + j / nqb;
       const int q0 = k0 + (j % nqb) * kB + qd * 32;  // first query row of this warp
       uint32_t v0[32], v1[32];
-      tmem_ld_32x32b_x32(tmem + lb + 384 + (j & 1) * kHD, v0);
-      tmem_ld_32x32b_x32(tmem + lb + 416 + (j & 1) * kHD, v1);
+      tmem_ld_32x32b_x32(tmem + lb + kColDQ, v0);
+      tmem_ld_32x32b_x32(tmem + lb + kColDQ + 32, v1);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dq_empty[j & 1]);
+      if (lane == 0) mbar_arrive(&dq_empty[0]);
       // rows past q_end hold exact zeros (their P is masked), so only whole-warp tails skip
       if (q0 < q_end) {
         // the MMAs of block j completed, so its P^T buffer is free until block j+2
@@ -386,7 +397,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = qd * 32 + lane;  // key row of S^T
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
     const int key = k0 + r;
-    bool ok = true;
+    bool ok = mbar_wait_warp(kv_full, 0, p.err, abort_flag);
+    if (ok) {
+      // row r of K (warps 4-7) or V (warps 12-15), 128B-swizzled in shared memory, as 32
+      // bf16 pairs into this row's TMEM lane: the A operand layout of the S^T / dP^T MMAs
+      const uint8_t* row = smem + (hf ? Smem::V : Smem::K) + r * 128;
+      uint32_t w[32];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) * 16));
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      tmem_st_32x32b_x32(tmem + lb + (hf ? kColV : kColK), w);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kv_tmem);
+    }
     for (int it = 0; it < n_it && ok; ++it) {
       // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed and the
       // dQ staging of that block has been read by the TMA
