@@ -18,12 +18,11 @@
 // warpgroup (warps 4-7: queries 0-63, warps 12-15: queries 64-127) and its own TMEM
 // full/empty barriers: a half's S^T / dP^T of the next block is computed as soon as that
 // warpgroup has read the current one, so the tensor core overlaps the softmax.
-// dQ of each block is added to an fp32 buffer by warps 8-11: they stage it, scaled, in the
-// block's P^T buffer (free once the block's MMAs completed, until the softmax of block+2 writes
-// it) as four 32-row x 64-column 128B-swizzled boxes, and each warp issues TMA reduce-adds of
-// its two [32 x 32] boxes, so the L2 adds whole lines; the warp releases the buffer to the
-// softmax once the TMA has read it.  dK and dV are complete at the end of the CTA (all q heads
-// of the group were visited) and are written once as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the
+// dQ of each block is added to an fp32 buffer by warps 8-11: each warp stages its 32 rows,
+// scaled, as two [32 x 32] 128B-swizzled boxes in its 4 KB share of V's shared memory (unused
+// once V is in TMEM) and issues a TMA reduce-add per box, so the L2 adds whole lines.  dK and
+// dV are complete at the end of the CTA (all q heads of the group were visited) and are written
+// once as bf16 -- no atomics.  A prologue kernel computes D = rowsum(dO * O) and the
 // sink gradient d(sink_h) = -sum_i exp(sink_h - lse_h(i)) * D_h(i); an epilogue kernel
 // converts dQ to bf16.
 #include "common.h"
@@ -184,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 9;     // [2] per query half
   uint64_t* s_empty = bars + 11;   // [2] per query half
   uint64_t* p_full = bars + 13;    // [2] P^T/dS^T buffer b written
-  uint64_t* pt_free = bars + 15;   // [2] P^T/dS^T buffer b consumed (MMAs, dQ staging read)
+  uint64_t* mma_done = bars + 15;  // [2] P^T/dS^T buffer b consumed
   uint64_t* dq_full = bars + 17;   // [2]
   uint64_t* dq_empty = bars + 19;  // [2]
   uint64_t* final_done = bars + 21;
@@ -220,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
       mbar_init(&p_full[s], 8);
-      mbar_init(&pt_free[s], 4);
+      mbar_init(&mma_done[s], 1);
       mbar_init(&dq_full[s], 1);   // only [0] is used
       mbar_init(&dq_empty[s], 4);  // only [0] is used: one dQ accumulator
     }
@@ -263,11 +262,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = g * rep + it / nqb;
       const int qb = k0 + (it % nqb) * kB;
       float* dst = reinterpret_cast<float*>(smem + Smem::LD + s * 2 * kB * 4);
-      for (int c = lane; c < kB; c += 32) {
-        const int qi = qb + c;
+      // all eight loads are in flight together (one memory latency per block, not four)
+      float lv[4], dv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int qi = qb + lane + 32 * k;
         const bool ok = qi < p.T;
-        dst[c] = ok ? p.lse[(int64_t)h * p.T + qi] * kLog2e : INFINITY;
-        dst[kB + c] = ok ? p.Dd[(int64_t)h * p.T + qi] : 0.f;
+        lv[k] = ok ? __ldg(p.lse + (int64_t)h * p.T + qi) * kLog2e : INFINITY;
+        dv[k] = ok ? __ldg(p.Dd + (int64_t)h * p.T + qi) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        dst[lane + 32 * k] = lv[k];
+        dst[kB + lane + 32 * k] = dv[k];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&ld_full[s]);
@@ -338,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
             umma_f16(tmem + kColDQ, a, b, id_q, kk > 0);
           }
+          umma_commit(&mma_done[j & 1]);
           umma_commit(&dq_full[0]);
           umma_commit(&qdo_empty[s]);
         }
@@ -362,32 +370,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&dq_empty[0]);
       // rows past q_end hold exact zeros (their P is masked), so only whole-warp tails skip
       if (q0 < q_end) {
-        // the MMAs of block j completed, so its P^T buffer is free until block j+2
-        uint8_t* stage = smem + Smem::PT + (j & 1) * kB * kB * 2 + qd * 8192;
+        uint8_t* stage = smem + Smem::V + qd * 4096;
         const uint32_t sw = smem_u32(stage) + lane * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t o = ((c ^ (lane & 7)) * 16);
-          st_shared_v4(sw + o, __float_as_uint(__uint_as_float(v0[4 * c]) * p.scale),
-                       __float_as_uint(__uint_as_float(v0[4 * c + 1]) * p.scale),
-                       __float_as_uint(__uint_as_float(v0[4 * c + 2]) * p.scale),
-                       __float_as_uint(__uint_as_float(v0[4 * c + 3]) * p.scale));
-          st_shared_v4(sw + 4096 + o, __float_as_uint(__uint_as_float(v1[4 * c]) * p.scale),
-                       __float_as_uint(__uint_as_float(v1[4 * c + 1]) * p.scale),
-                       __float_as_uint(__uint_as_float(v1[4 * c + 2]) * p.scale),
-                       __float_as_uint(__uint_as_float(v1[4 * c + 3]) * p.scale));
+        for (int half = 0; half < 2; ++half) {
+          // the TMA has read the previous box out of this warp's staging area
+          if (lane == 0) bulk_wait_read();
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t* v = half ? v1 : v0;
+            st_shared_v4(sw + ((c ^ (lane & 7)) * 16),
+                         __float_as_uint(__uint_as_float(v[4 * c]) * p.scale),
+                         __float_as_uint(__uint_as_float(v[4 * c + 1]) * p.scale),
+                         __float_as_uint(__uint_as_float(v[4 * c + 2]) * p.scale),
+                         __float_as_uint(__uint_as_float(v[4 * c + 3]) * p.scale));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&tma_dq, stage, h * kHD + half * 32, q0);
+            bulk_commit();
+          }
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_reduce_add_2d(&tma_dq, stage, h * kHD, q0);
-          tma_reduce_add_2d(&tma_dq, stage + 4096, h * kHD + 32, q0);
-          bulk_commit();
-          bulk_wait_read();
-        }
-        __syncwarp();
       }
-      if (lane == 0) mbar_arrive(&pt_free[j & 1]);
     }
     if (lane == 0) bulk_wait_all();
   } else if (warp >= 4) {
@@ -418,9 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(kv_tmem);
     }
     for (int it = 0; it < n_it && ok; ++it) {
-      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed and the
-      // dQ staging of that block has been read by the TMA
-      if (it >= 2 && !mbar_wait_warp(&pt_free[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
+      if (it >= 2 && !mbar_wait_warp(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
