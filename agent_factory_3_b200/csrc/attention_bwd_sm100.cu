@@ -1,23 +1,25 @@
 // Flash-attention backward for gpt-oss on sm_100a (causal GQA, packed varlen, sliding
 // window, learned sinks, head_dim 64).
 //
-// One CTA per (128-key tile, kv head).  It keeps K and V of its key tile in shared memory and
-// loops over every q head of the kv group and every 128-query block that can see the tile:
+// One CTA per (128-key tile, kv head).  It keeps K and V of its key tile on chip and loops
+// over every q head of the kv group and every 128-query block that can see the tile, in two
+// 64-query halves per block:
 //   S^T  = K Q^T        (tcgen05, M=128 keys, N=64 queries per half, K=64)  TMEM cols   0..127
 //   dP^T = V dO^T       (same shape)                                        TMEM cols 128..255
-//          K and V are the A operands of these two products and are read from TMEM (cols
-//          448..479 and 480..511, copied there once per CTA): with N = 64, an MMA that reads
-//          both operands from shared memory is bound by shared-memory bandwidth, and shared
-//          memory is the busiest unit of this kernel.
 //   P^T  = 2^(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - D[q])   (softmax warps,
-//          thread = key row, written as bf16 into 128B-swizzled shared memory)
-//   dV  += P^T dO       (A = P^T K-major, B = dO as MN-major)         TMEM cols 256..319
-//   dK  += dS^T Q       (A = dS^T, B = Q as MN-major)                 TMEM cols 320..383
-//   dQ   = dS K         (A = dS^T read as MN-major, B = K as MN-major) TMEM cols 384..447
-// The 128 query columns of S^T / dP^T are split into two halves, each with its own softmax
-// warpgroup (warps 4-7: queries 0-63, warps 12-15: queries 64-127) and its own TMEM
-// full/empty barriers: a half's S^T / dP^T of the next block is computed as soon as that
-// warpgroup has read the current one, so the tensor core overlaps the softmax.
+//          thread = key row; written back as bf16 pairs over the S^T / dP^T columns they
+//          were computed from, and dS^T also into 128B-swizzled shared memory)
+//   dV  += P^T dO       (A = P^T from TMEM, B = dO as MN-major)        TMEM cols 256..319
+//   dK  += dS^T Q       (A = dS^T from TMEM, B = Q as MN-major)        TMEM cols 320..383
+//   dQ   = dS K         (A = dS^T read as MN-major from shared memory, B = K as MN-major)
+//                                                                      TMEM cols 384..447
+// K and V are the A operands of S^T / dP^T and sit in TMEM too (cols 448..479, 480..511,
+// copied there once per CTA).  With N = 64 an MMA that reads both operands from shared memory
+// is bound by shared-memory bandwidth, the busiest unit of this kernel, so every product except
+// dQ takes its A operand from TMEM and reads only the 2 KB B slice per instruction.
+// The eight softmax warps work on one half at a time (warp quarter = 32 key rows, warps 4-7
+// the first 32 queries of the half, warps 12-15 the other 32); while they compute one half,
+// the tensor core runs dV / dK of the other half and the next block's S^T / dP^T of it.
 // dQ of each block is added to an fp32 buffer by warps 8-11: each warp stages its 32 rows,
 // scaled, as two [32 x 32] 128B-swizzled boxes in its 4 KB share of V's shared memory (unused
 // once V is in TMEM) and issues a TMA reduce-add per box, so the L2 adds whole lines.  dK and
@@ -44,11 +46,10 @@ struct Smem {
   static constexpr int K = 0;                         // 16 KB  [128 keys x 64] K-major
   static constexpr int V = K + kB * kHD * 2;          // 16 KB
   static constexpr int QDO = V + kB * kHD * 2;        // 2 stages x (Q 16 KB + dO 16 KB)
-  static constexpr int PT = QDO + 2 * 2 * kB * kHD * 2;   // 2 x 32 KB P^T (double buffered)
-  static constexpr int DST = PT + 2 * kB * kB * 2;    // 2 x 32 KB dS^T
+  static constexpr int DST = QDO + 2 * 2 * kB * kHD * 2;  // 2 x 32 KB dS^T (double buffered)
   static constexpr int LD = DST + 2 * kB * kB * 2;    // 2 stages x (lse2 512 B + D 512 B)
   static constexpr int BAR = LD + 2 * 2 * kB * 4;
-  static constexpr int TOTAL = BAR + 1024;            // 227 KB: the whole per-CTA budget
+  static constexpr int TOTAL = BAR + 1024;            // 163 KB
 };
 
 struct Params {
@@ -168,12 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tma_do,
                     const __grid_constant__ CUtensorMap tma_dq, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // the layout uses all 227 KB, so there is no slack to realign: require a 1024-aligned base
-  uint8_t* smem = smem_raw;
-  if ((smem_u32(smem) & 1023) != 0) {
-    if (threadIdx.x == 0) atomicExch(p.err, kErrBadShape);
-    return;
-  }
+  // the 128B-swizzled tiles need a 1024-aligned base; the launch adds 1 KB of slack for it
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::BAR);
   uint64_t* kv_full = bars + 0;
   uint64_t* qdo_full = bars + 1;   // [2]
@@ -181,9 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* ld_full = bars + 5;    // [2]
   uint64_t* ld_empty = bars + 7;   // [2]
   uint64_t* s_full = bars + 9;     // [2] per query half
-  uint64_t* s_empty = bars + 11;   // [2] per query half
-  uint64_t* p_full = bars + 13;    // [2] P^T/dS^T buffer b written
-  uint64_t* mma_done = bars + 15;  // [2] P^T/dS^T buffer b consumed
+  uint64_t* p_full = bars + 13;    // [2] per query half: P^T / dS^T of the half written
+  uint64_t* mma_done = bars + 15;  // [2] dS^T buffer b consumed
   uint64_t* dq_full = bars + 17;   // [2]
   uint64_t* dq_empty = bars + 19;  // [2]
   uint64_t* final_done = bars + 21;
@@ -217,7 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ld_full[s], 1);
       mbar_init(&ld_empty[s], 8);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);
       mbar_init(&p_full[s], 8);
       mbar_init(&mma_done[s], 1);
       mbar_init(&dq_full[s], 1);   // only [0] is used
@@ -281,74 +276,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer --------------------------------------
+    // Work goes in half-steps u = 2*it + hf (block it, query half hf).  For each u, once the
+    // softmax has written P^T / dS^T of the half into TMEM (over the S^T / dP^T columns it
+    // read): dV += P^T dO_hf and dK += dS^T Q_hf (A from TMEM), then S^T / dP^T of the same
+    // half of block it+1 into the same columns; after half 1, dQ of block it.  The tensor pipe
+    // runs one CTA's MMAs in issue order, so S(u+2) overwrites the columns only after
+    // dV / dK(u) read them.
     if (elect_one_sync()) {
       constexpr uint32_t id_s = make_idesc_bf16(kB, kB / 2, false, false);  // S^T, dP^T halves
       constexpr uint32_t id_kv = make_idesc_bf16(kB, kHD, false, true);     // dV, dK
       constexpr uint32_t id_q = make_idesc_bf16(kB, kHD, true, true);       // dQ
       const uint32_t sK = smem_u32(smem + Smem::K);
-      const uint32_t sPT = smem_u32(smem + Smem::PT), sDS = smem_u32(smem + Smem::DST);
+      const uint32_t sDS = smem_u32(smem + Smem::DST);
+      auto issue_s = [&](int it, int hf) {
+        const uint32_t sQ = smem_u32(smem + Smem::QDO + (it & 1) * 2 * kB * kHD * 2);
+        const uint32_t sDO = sQ + kB * kHD * 2;
+        // queries hf*64 .. hf*64+63 start 64 rows (8 KB, swizzle-atom aligned) in
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          umma_f16_tmem_a(tmem + hf * 64, tmem + kColK + kk * 8,
+                          make_smem_desc(sQ + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
+                          id_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          umma_f16_tmem_a(tmem + 128 + hf * 64, tmem + kColV + kk * 8,
+                          make_smem_desc(sDO + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
+                          id_s, kk > 0);
+        }
+        umma_commit(&s_full[hf]);
+      };
       bool ok = mbar_wait(kv_tmem, 0, p.err, abort_flag);
       tc_fence_after();
-      for (int it = 0; ok && it <= n_it; ++it) {
-        if (it < n_it) {
-          const int s = it & 1;
-          if (!mbar_wait(&qdo_full[s], (it >> 1) & 1, p.err, abort_flag)) break;
-          const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
-          const uint32_t sDO = sQ + kB * kHD * 2;
-          for (int hf = 0; hf < 2 && ok; ++hf) {
-            if (!mbar_wait(&s_empty[hf], (it & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            // queries hf*64 .. hf*64+63 start 64 rows (8 KB, swizzle-atom aligned) in
-#pragma unroll
-            for (int kk = 0; kk < kHD / 16; ++kk) {
-              umma_f16_tmem_a(tmem + hf * 64, tmem + kColK + kk * 8,
-                              make_smem_desc(sQ + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
-                              id_s, kk > 0);
-            }
-#pragma unroll
-            for (int kk = 0; kk < kHD / 16; ++kk) {
-              umma_f16_tmem_a(tmem + 128 + hf * 64, tmem + kColV + kk * 8,
-                              make_smem_desc(sDO + hf * 8192 + kk * 32, 16, 1024, kLayoutSW128),
-                              id_s, kk > 0);
-            }
-            umma_commit(&s_full[hf]);
-          }
-          if (!ok) break;
-        }
-        if (it >= 1) {
-          const int j = it - 1;
-          const int s = j & 1;
-          if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err, abort_flag)) break;
-          // the drain has read the previous block's dQ out of TMEM
-          if (!mbar_wait(&dq_empty[0], (j & 1) ^ 1, p.err, abort_flag)) break;
+      if (ok && n_it > 0) {
+        ok = mbar_wait(&qdo_full[0], 0, p.err, abort_flag);
+        if (ok) {
           tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
-          const uint32_t sDO = sQ + kB * kHD * 2;
-          const uint32_t sPTb = sPT + (j & 1) * kB * kB * 2;
-          const uint32_t sDSb = sDS + (j & 1) * kB * kB * 2;
-#pragma unroll
-          for (int kk = 0; kk < kB / 16; ++kk) {
-            // reduction over the 128 queries of the block
-            const uint64_t a_pt = make_smem_desc(sPTb + (kk / 4) * 16384 + (kk % 4) * 32, 16,
-                                                 1024, kLayoutSW128);
-            const uint64_t a_ds = make_smem_desc(sDSb + (kk / 4) * 16384 + (kk % 4) * 32, 16,
-                                                 1024, kLayoutSW128);
-            const uint64_t b_do = make_smem_desc(sDO + kk * 2048, 8192, 1024, kLayoutSW128);
-            const uint64_t b_q = make_smem_desc(sQ + kk * 2048, 8192, 1024, kLayoutSW128);
-            umma_f16(tmem + 256, a_pt, b_do, id_kv, (j > 0 || kk > 0) ? 1u : 0u);
-            umma_f16(tmem + 320, a_ds, b_q, id_kv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < kB / 16; ++kk) {
-            // reduction over the 128 keys: A = dS (M = queries) read from dS^T as MN-major
-            const uint64_t a = make_smem_desc(sDSb + kk * 2048, 16384, 1024, kLayoutSW128);
-            const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
-            umma_f16(tmem + kColDQ, a, b, id_q, kk > 0);
-          }
-          umma_commit(&mma_done[j & 1]);
-          umma_commit(&dq_full[0]);
-          umma_commit(&qdo_empty[s]);
+          issue_s(0, 0);
+          issue_s(0, 1);
         }
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int s = it & 1;
+        const uint32_t sQ = smem_u32(smem + Smem::QDO + s * 2 * kB * kHD * 2);
+        const uint32_t sDO = sQ + kB * kHD * 2;
+        for (int hf = 0; hf < 2 && ok; ++hf) {
+          if (!mbar_wait(&p_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // queries hf*64 + 16*kk .. +15: P^T / dS^T pairs at column (kk/2)*32 + (kk%2)*8
+            // of the half (each softmax warp writes its 32 queries over its own S columns)
+            const uint32_t col = hf * 64 + (kk >> 1) * 32 + (kk & 1) * 8;
+            const uint64_t b_do = make_smem_desc(sDO + (hf * 4 + kk) * 2048, 8192, 1024, kLayoutSW128);
+            const uint64_t b_q = make_smem_desc(sQ + (hf * 4 + kk) * 2048, 8192, 1024, kLayoutSW128);
+            const uint32_t acc = (it > 0 || hf > 0 || kk > 0) ? 1u : 0u;
+            umma_f16_tmem_a(tmem + 256, tmem + col, b_do, id_kv, acc);
+            umma_f16_tmem_a(tmem + 320, tmem + 128 + col, b_q, id_kv, acc);
+          }
+          if (it + 1 < n_it) {
+            if (hf == 0) {
+              if (!mbar_wait(&qdo_full[(it + 1) & 1], ((it + 1) >> 1) & 1, p.err, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            issue_s(it + 1, hf);
+          }
+        }
+        if (!ok) break;
+        // dQ of block it: reduction over the 128 keys, A = dS (M = queries) read from dS^T in
+        // shared memory as MN-major; the drain has read the previous block's dQ out of TMEM
+        if (!mbar_wait(&dq_empty[0], (it & 1) ^ 1, p.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t sDSb = sDS + s * kB * kB * 2;
+#pragma unroll
+        for (int kk = 0; kk < kB / 16; ++kk) {
+          const uint64_t a = make_smem_desc(sDSb + kk * 2048, 16384, 1024, kLayoutSW128);
+          const uint64_t b = make_smem_desc(sK + kk * 2048, 8192, 1024, kLayoutSW128);
+          umma_f16(tmem + kColDQ, a, b, id_q, kk > 0);
+        }
+        umma_commit(&mma_done[s]);
+        umma_commit(&dq_full[0]);
+        umma_commit(&qdo_empty[s]);
       }
       if (ok) umma_commit(final_done);
     }
@@ -397,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) bulk_wait_all();
   } else if (warp >= 4) {
-    // ---------------- softmax gradient (P^T, dS^T) of one half of the queries ----------
-    const int hf = warp >= 12 ? 1 : 0;
+    // ------ softmax gradient: key rows of quarter qd, query columns cg*32.. of each half ------
+    const int cg = warp >= 12 ? 1 : 0;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // key row of S^T
     const uint32_t lb = (uint32_t)(qd * 32) << 16;
@@ -407,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       // row r of K (warps 4-7) or V (warps 12-15), 128B-swizzled in shared memory, as 32
       // bf16 pairs into this row's TMEM lane: the A operand layout of the S^T / dP^T MMAs
-      const uint8_t* row = smem + (hf ? Smem::V : Smem::K) + r * 128;
+      const uint8_t* row = smem + (cg ? Smem::V : Smem::K) + r * 128;
       uint32_t w[32];
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -417,87 +428,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         w[4 * c + 2] = v.z;
         w[4 * c + 3] = v.w;
       }
-      tmem_st_32x32b_x32(tmem + lb + (hf ? kColV : kColK), w);
+      tmem_st_32x32b_x32(tmem + lb + (cg ? kColV : kColK), w);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(kv_tmem);
     }
     for (int it = 0; it < n_it && ok; ++it) {
-      // buffer it&1 is free once the MMAs of block it-2 (its previous user) completed
-      if (it >= 2 && !mbar_wait_warp(&mma_done[it & 1], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
+      const int s = it & 1;
+      // dS^T buffer s is free once the MMAs of block it-2 (its previous user) completed
+      if (it >= 2 && !mbar_wait_warp(&mma_done[s], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
-      const int s = it & 1;
       if (!mbar_wait_warp(&ld_full[s], (it >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-      if (!mbar_wait_warp(&s_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
-      tc_fence_after();
       const float* lds = reinterpret_cast<const float*>(smem + Smem::LD + s * 2 * kB * 4);  // lse2, D
       const int qb = k0 + (it % nqb) * kB;
-      const uint32_t pt = smem_u32(smem + Smem::PT + (it & 1) * kB * kB * 2);
-      const uint32_t ds = smem_u32(smem + Smem::DST + (it & 1) * kB * kB * 2);
-      // four 16-query chunks; the TMEM loads of chunk q+1 are in flight while chunk q computes
-      uint32_t sA[16], dA[16], sB[16], dB[16];
-      tmem_ld_32x32b_x16(tmem + lb + hf * 64, sA);
-      tmem_ld_32x32b_x16(tmem + lb + 128 + hf * 64, dA);
-      tmem_ld_wait();
+      const uint32_t ds = smem_u32(smem + Smem::DST + s * kB * kB * 2);
+      for (int hf = 0; hf < 2; ++hf) {
+        if (!mbar_wait_warp(&s_full[hf], it & 1, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const int c0 = hf * 64 + cg * 32;      // first query column of this warp
+        const uint32_t col = tmem + lb + c0;   // its S^T columns; dP^T 128 columns on
+        uint32_t sA[16], dA[16], sB[16], dB[16];
+        tmem_ld_32x32b_x16(col, sA);
+        tmem_ld_32x32b_x16(col + 128, dA);
+        tmem_ld_32x32b_x16(col + 16, sB);
+        tmem_ld_32x32b_x16(col + 128 + 16, dB);
+        tmem_ld_wait();
+        uint32_t p0[8], d0[8], p1[8], d1[8];
+        const bool vis0 = key < k1 && key <= qb + c0 && qb + c0 + 15 < q_end &&
+                          (p.window == 0 || qb + c0 + 15 - key < p.window);
+        const bool vis1 = key < k1 && key <= qb + c0 + 16 && qb + c0 + 31 < q_end &&
+                          (p.window == 0 || qb + c0 + 31 - key < p.window);
+        if (vis0)
+          softmax_grad16<false>(sA, dA, lds, c0, p.scale_log2, key, qb, k1, q_end, p.window, p0, d0);
+        else
+          softmax_grad16<true>(sA, dA, lds, c0, p.scale_log2, key, qb, k1, q_end, p.window, p0, d0);
+        if (vis1)
+          softmax_grad16<false>(sB, dB, lds, c0 + 16, p.scale_log2, key, qb, k1, q_end, p.window, p1, d1);
+        else
+          softmax_grad16<true>(sB, dB, lds, c0 + 16, p.scale_log2, key, qb, k1, q_end, p.window, p1, d1);
+        // P^T / dS^T of the 32 queries as bf16 pairs over this warp's first 16 S^T / dP^T
+        // columns (already read): the TMEM A operands of the dV / dK MMAs
+        uint32_t wp[16], wd[16];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int c = hf * 64 + q * 16;  // query column of this chunk
-        if (q < 3) {
-          if (q % 2 == 0) {
-            tmem_ld_32x32b_x16(tmem + lb + c + 16, sB);
-            tmem_ld_32x32b_x16(tmem + lb + 128 + c + 16, dB);
-          } else {
-            tmem_ld_32x32b_x16(tmem + lb + c + 16, sA);
-            tmem_ld_32x32b_x16(tmem + lb + 128 + c + 16, dA);
-          }
+        for (int e = 0; e < 8; ++e) {
+          wp[e] = p0[e];
+          wp[8 + e] = p1[e];
+          wd[e] = d0[e];
+          wd[8 + e] = d1[e];
         }
-        const bool all_vis = key < k1 && key <= qb + c && qb + c + 15 < q_end &&
-                             (p.window == 0 || qb + c + 15 - key < p.window);
-        uint32_t pp[8], dd[8];
-        if (q % 2 == 0) {
-          if (all_vis)
-            softmax_grad16<false>(sA, dA, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
-          else
-            softmax_grad16<true>(sA, dA, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
-        } else {
-          if (all_vis)
-            softmax_grad16<false>(sB, dB, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
-          else
-            softmax_grad16<true>(sB, dB, lds, c, p.scale_log2, key, qb, k1, q_end, p.window, pp, dd);
-        }
-        store_sw128(pt, r, c / 8, pp[0], pp[1], pp[2], pp[3]);
-        store_sw128(pt, r, c / 8 + 1, pp[4], pp[5], pp[6], pp[7]);
-        store_sw128(ds, r, c / 8, dd[0], dd[1], dd[2], dd[3]);
-        store_sw128(ds, r, c / 8 + 1, dd[4], dd[5], dd[6], dd[7]);
-        if (q < 3) {
-          tmem_ld_wait();
-          if (q == 2) {   // every S^T / dP^T column of this half is in registers
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[hf]);
-          }
-        }
+        tmem_st_32x32b_x16(col, wp);
+        tmem_st_32x32b_x16(col + 128, wd);
+        // dS^T in shared memory: the A operand of the dQ MMA
+        store_sw128(ds, r, c0 / 8, d0[0], d0[1], d0[2], d0[3]);
+        store_sw128(ds, r, c0 / 8 + 1, d0[4], d0[5], d0[6], d0[7]);
+        store_sw128(ds, r, c0 / 8 + 2, d1[0], d1[1], d1[2], d1[3]);
+        store_sw128(ds, r, c0 / 8 + 3, d1[4], d1[5], d1[6], d1[7]);
+        tmem_st_wait();
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[hf]);
       }
-      fence_proxy_async_smem();
+      if (!ok) break;
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&ld_empty[s]);
-        mbar_arrive(&p_full[it & 1]);
-      }
+      if (lane == 0) mbar_arrive(&ld_empty[s]);
     }
     if (ok && mbar_wait(final_done, 0, p.err, abort_flag)) {
-      // half 0 writes dV, half 1 writes dK
+      // warps 4-7 write dV, warps 12-15 write dK
       tc_fence_after();
       uint32_t a0[32], a1[32];
-      tmem_ld_32x32b_x32(tmem + lb + 256 + hf * 64, a0);
-      tmem_ld_32x32b_x32(tmem + lb + 288 + hf * 64, a1);
+      tmem_ld_32x32b_x32(tmem + lb + 256 + cg * 64, a0);
+      tmem_ld_32x32b_x32(tmem + lb + 288 + cg * 64, a1);
       tmem_ld_wait();
       if (key < k1) {
-        const float sc = hf ? p.scale : 1.f;
-        __nv_bfloat16* dst = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + (hf ? 0 : p.hkv) + g) * kHD;
+        const float sc = cg ? p.scale : 1.f;
+        __nv_bfloat16* dst = p.dqkv + (int64_t)key * p.ld_dqkv + (p.hq + (cg ? 0 : p.hkv) + g) * kHD;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           float t[8];
@@ -618,7 +626,7 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
   p.scale = (float)scale;
   p.scale_log2 = (float)scale * kLog2e;
   p.err = device_error_ptr();
-  const int smem = Smem::TOTAL;
+  const int smem = Smem::TOTAL + 1024;
   static bool attr[64] = {};
   int dev;
   AF3_CUDA_CHECK(cudaGetDevice(&dev));
