@@ -108,9 +108,9 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
@@ -125,9 +125,9 @@ __device__ __forceinline__ uint32_t bf16x2_of(float lo, float hi) {
 }
 
 // P^T and dS^T of one key row over 16 query columns starting at c, as bf16 pairs (packed
-// fp32x2 arithmetic).  lse2 (log2 domain) and D of the block's queries are in shared memory at
-// lds (lse2[128] then D[128]); every lane reads the same addresses, so the 16-byte loads are
-// broadcasts.
+// fp32x2 arithmetic).  -lse2 (log2 domain, negated so that it is the FMA's addend as loaded)
+// and D of the block's queries are in shared memory at lds (-lse2[128] then D[128]); every
+// lane reads the same addresses, so the 16-byte loads are broadcasts.
 template <bool MASK>
 __device__ __forceinline__ void softmax_grad16(const uint32_t (&sv)[16], const uint32_t (&dv)[16],
                                                const float* lds, int c, float scale_log2, int key,
@@ -145,7 +145,7 @@ __device__ __forceinline__ void softmax_grad16(const uint32_t (&sv)[16], const u
       const float da = h2 ? d4.z : d4.x, db = h2 ? d4.w : d4.y;
       float t0, t1;
       f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc2,
-                       f2_pack(-la, -lb)), t0, t1);
+                       f2_pack(la, lb)), t0, t1);
       float p0 = ex2(t0), p1 = ex2(t1);
       if (MASK) {
         const int q0 = qb + c + e, q1 = q0 + 1;
@@ -156,8 +156,8 @@ __device__ __forceinline__ void softmax_grad16(const uint32_t (&sv)[16], const u
       }
       float s0, s1;
       f2_unpack(f2_mul(f2_pack(p0, p1),
-                       f2_add(f2_pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
-                              f2_pack(-da, -db))), s0, s1);
+                       f2_sub(f2_pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+                              f2_pack(da, db))), s0, s1);
       pp[e / 2] = bf16x2_of(p0, p1);
       dd[e / 2] = bf16x2_of(s0, s1);
     }
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) {
         const int qi = qb + lane + 32 * k;
         const bool ok = qi < p.T;
-        lv[k] = ok ? __ldg(p.lse + (int64_t)h * p.T + qi) * kLog2e : INFINITY;
+        lv[k] = ok ? __ldg(p.lse + (int64_t)h * p.T + qi) * -kLog2e : -INFINITY;
         dv[k] = ok ? __ldg(p.Dd + (int64_t)h * p.T + qi) : 0.f;
       }
 #pragma unroll
