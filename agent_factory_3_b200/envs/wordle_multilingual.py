@@ -7,12 +7,13 @@ mcp_tools/wordle_multilingual/{core,server_en,server_ja,server_zh}.py).
 * ``zh``: 5-symbol zhuyin (bopomofo) spellings without tones, shown with their Chinese words.
 
 The ja / zh dictionaries are JSON objects ``{spelling: [word, ...]}`` — ``answer_dict.json``
-(answer pool) and ``valid_dict.json`` (every accepted guess); they are not bundled and are
-passed with ``--data-dir``.  Every guess costs an attempt (invalid ones included); feedback is
+(answer pool) and ``valid_dict.json`` (every accepted guess).  The package bundles the
+reference's dictionaries (``envs/data/wordle_ja``, ``envs/data/wordle_zh``: 1839 / 1450
+answers); ``--data-dir`` points at another pair.  Every guess costs an attempt (invalid ones included); feedback is
 ``correct`` / ``present`` / ``absent`` per character with duplicates resolved by the two-pass
 rule; ``early_exit`` is set when the game ends.
 
-    python -m agent_factory_3_b200.envs.wordle_multilingual --lang ja --data-dir DIR --seed 3
+    python -m agent_factory_3_b200.envs.wordle_multilingual --lang ja --seed 3
 """
 from __future__ import annotations
 
@@ -80,7 +81,7 @@ def make_game(lang: str, data_dir: Path | None = None, target: str | None = None
             raise ValueError(f"target {target!r} is not in the answers list")
         return WordleGame(target, load_words(DATA / "wordle_allowed.txt") | set(answers))
     if data_dir is None:
-        raise ValueError(f"lang {lang!r} needs --data-dir with answer_dict.json and valid_dict.json")
+        data_dir = DATA / f"wordle_{lang}"
     answers = load_dict(Path(data_dir) / "answer_dict.json")
     valid = load_dict(Path(data_dir) / "valid_dict.json")
     pool = sorted(answers)

@@ -75,7 +75,13 @@ def test_wordle_multilingual(tmp_path):
     srv = WM.build_server("ja", data_dir=d, target="あたらしい")
     assert _call(srv, "guess", {"word": "あたらしい"})["early_exit"] is True
     with pytest.raises(ValueError):
-        WM.make_game("zh")
+        WM.make_game("fr")
+    # the bundled dictionaries: every answer is a 5-symbol spelling that is also a valid guess
+    for lang in ("ja", "zh"):
+        g = WM.make_game(lang, seed=5)
+        assert len(g.answer) == 5
+        r = g.guess(g.answer)
+        assert r["won"] and r["answer"].startswith(g.answer)
 
 
 # ------------------------------------------------------------------ sokoban
