@@ -531,26 +531,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // D[h, i] = sum_d dO[i, h, d] * O[i, h, d]; dsink[h] -= exp(sink_h - lse[h, i]) * D[h, i].
-// One warp per (row, head) pair; head_dim 64 = 2 elements per lane.
-__global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, int64_t ld_out,
-                                    const __nv_bfloat16* __restrict__ dout, int64_t ld_dout,
-                                    const float* __restrict__ lse, const float* __restrict__ sinks,
-                                    float* __restrict__ Dd, float* __restrict__ dsink, int T,
-                                    int hq) {
-  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
-  if (w >= (int64_t)T * hq) return;
-  const int h = (int)(w % hq);
-  const int64_t i = w / hq;
-  const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(out + i * ld_out + h * kHD)[lane];
-  const __nv_bfloat162 d = reinterpret_cast<const __nv_bfloat162*>(dout + i * ld_dout + h * kHD)[lane];
-  const float2 of = __bfloat1622float2(o), df = __bfloat1622float2(d);
-  float s = of.x * df.x + of.y * df.y;
+// One block per kPreRows rows; warp w takes heads w, w + 8, ... and walks the block's rows
+// (head_dim 64 = 2 elements per lane), summing its sink-gradient terms in a register: one
+// atomic per (block, head) instead of one per (row, head), which serialised on the hq words.
+constexpr int kPreRows = 64;
+__global__ void __launch_bounds__(256)
+    attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out, int64_t ld_out,
+                        const __nv_bfloat16* __restrict__ dout, int64_t ld_dout,
+                        const float* __restrict__ lse, const float* __restrict__ sinks,
+                        float* __restrict__ Dd, float* __restrict__ dsink, int T, int hq) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t r0 = (int64_t)blockIdx.x * kPreRows;
+  const int rows = T - r0 < kPreRows ? (int)(T - r0) : kPreRows;
+  for (int h = warp; h < hq; h += 8) {
+    const float sk = sinks[h];
+    float acc = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < rows; ++k) {
+      const int64_t i = r0 + k;
+      const __nv_bfloat162 o =
+          reinterpret_cast<const __nv_bfloat162*>(out + i * ld_out + h * kHD)[lane];
+      const __nv_bfloat162 d =
+          reinterpret_cast<const __nv_bfloat162*>(dout + i * ld_dout + h * kHD)[lane];
+      const float2 of = __bfloat1622float2(o), df = __bfloat1622float2(d);
+      float s = of.x * df.x + of.y * df.y;
 #pragma unroll
-  for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffff, s, k);
-  if (lane == 0) {
-    Dd[(int64_t)h * T + i] = s;
-    atomicAdd(&dsink[h], -__expf(sinks[h] - lse[(int64_t)h * T + i]) * s);
+      for (int m = 16; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffff, s, m);
+      if (lane == 0) {
+        Dd[(int64_t)h * T + i] = s;
+        acc -= __expf(sk - lse[(int64_t)h * T + i]) * s;
+      }
+    }
+    if (lane == 0) atomicAdd(&dsink[h], acc);
   }
 }
 
@@ -589,8 +601,7 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor sinks, torch::Tensor kv_tiles, to
   auto Dd = torch::empty({hq, T}, qkv.options().dtype(torch::kFloat32));
   auto dq = torch::zeros({T, hq * kHD}, qkv.options().dtype(torch::kFloat32));
   {
-    const int64_t warps = T * hq;
-    attn_bwd_pre_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
+    attn_bwd_pre_kernel<<<(unsigned)((T + kPreRows - 1) / kPreRows), 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
         lse.data_ptr<float>(), sinks.data_ptr<float>(), Dd.data_ptr<float>(),
