@@ -253,13 +253,21 @@ class ModelTrainer(RPCMixin):
         extra = torch.stack([loss_sum.detach().float(),
                              grad_norm.float() if grad_norm is not None else torch.zeros((), device=self.device)])
         red = all_reduce_metric_states(states, extra=extra)
-        vals = red.tolist()  # the step's single device->host read
-        self.last_step_d2h_bytes = 4 * (len(vals) + len(states))
+        keys = sorted(states)
+        # the reduced extras and every metric's mean in one tensor: the step's single
+        # device->host read
+        packed = [red.float().reshape(-1)]
+        if keys:
+            packed.append(torch.stack([(states[k].sum / states[k].count.clamp_min(1.0)).float()
+                                       for k in keys]))
+        host = torch.cat(packed).tolist()
+        self.last_step_d2h_bytes = 4 * len(host)
+        vals = host[:red.numel()]
         metrics = {"loss": vals[0], "learning_rate": float(self.optimizer.param_groups[0]["lr"])}
         if grad_norm is not None:
             metrics["grad_norm"] = vals[1] / self.world_size  # every rank holds the global norm
-        for k, st in states.items():
-            metrics[k] = float((st.sum / st.count.clamp_min(1.0)).item())
+        for k, v in zip(keys, host[red.numel():]):
+            metrics[k] = float(v)
         return metrics
 
     def train_step(self, step_samples: list[TrainingSample]) -> dict[str, float]:
