@@ -18,10 +18,11 @@ from ..types import TrainingSample
 
 class DataCollatorWithPacking:
     def __init__(self, pad_token_id: int = 0, pad_to_multiple_of: int = 128, pin_memory: bool = False,
-                 vocab_size: int | None = None):
+                 vocab_size: int | None = None, num_experts: int | None = None):
         if vocab_size is not None and not 0 <= pad_token_id < vocab_size:
             raise ValueError(f"pad_token_id {pad_token_id} outside vocabulary of {vocab_size}")
         self.vocab_size = vocab_size
+        self.num_experts = num_experts
         self.pad_token_id = pad_token_id
         self.pad_to_multiple_of = pad_to_multiple_of
         self.pin_memory = pin_memory
@@ -79,6 +80,12 @@ class DataCollatorWithPacking:
             for s, n in zip(samples, lens):
                 rt[off:off + n] = get(s, "routing_indices")
                 off += n
+            # replayed ids index the router logits and the expert histograms on the device, so
+            # an id outside [0, num_experts) is rejected here, on the host; saved batches mark
+            # positions without a recorded route with 255, which must be filled before training
+            if self.num_experts is not None and rt.size and int(rt.max()) >= self.num_experts:
+                raise ValueError(f"routing id {int(rt.max())} outside [0, {self.num_experts}) in "
+                                 "the batch (255 marks an unrecorded position in saved batches)")
             batch["routing_indices"] = rt
         if not isinstance(samples[0], dict) or "divisor" in samples[0]:
             batch["divisor"] = np.array([get(s, "divisor") or 1.0 for s in samples], np.float32)

@@ -111,7 +111,8 @@ class ModelTrainer(RPCMixin):
         self.collator = DataCollatorWithPacking(pad_token_id=self.model.cfg.pad_token_id,
                                                 pad_to_multiple_of=config.pad_to_multiple_of_training,
                                                 pin_memory=self.device.type == "cuda",
-                                                vocab_size=self.model.cfg.vocab_size)
+                                                vocab_size=self.model.cfg.vocab_size,
+                                                num_experts=self.model.cfg.num_local_experts)
         self.step_count = 0
         self.last_step_events = None
         self._outbox = None

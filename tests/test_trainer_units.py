@@ -58,6 +58,13 @@ def test_collator_packing():
     assert b["routing_indices"].shape == (12, L, K) and int(b["routing_indices"][7, 0, 0]) == 2
     with pytest.raises(ValueError):
         DataCollatorWithPacking(vocab_size=4)([s1])
+    # replayed routing ids must index real experts: the saved-batch sentinel 255 is rejected
+    assert DataCollatorWithPacking(num_experts=3)([s1, s2])["routing_indices"].shape[1:] == (L, K)
+    with pytest.raises(ValueError, match="255"):
+        DataCollatorWithPacking(num_experts=2)([s1, s2])
+    bad = _sample(3, 1, "c", lr=np.full((3, L, K), 255, np.uint8))
+    with pytest.raises(ValueError):
+        DataCollatorWithPacking(num_experts=128)([s1, bad])
 
 
 def test_packed_sampler_best_fit_and_zigzag():
