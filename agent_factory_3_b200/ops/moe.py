@@ -76,6 +76,12 @@ def group_reference(ids: torch.Tensor, gates: torch.Tensor, n_experts: int) -> R
 def route(logits: torch.Tensor, top_k: int, n_experts: int,
           replay_ids: torch.Tensor | None = None) -> Routing:
     """Router top-k (or replay of recorded ids) + grouping, without host synchronisation."""
+    if replay_ids is not None and not replay_ids.is_cuda and replay_ids.numel():
+        # ids still on the host are checked before they index logits and histograms on the
+        # device (ids already on the device were checked where they were collated)
+        lo, hi = int(replay_ids.min()), int(replay_ids.max())
+        if lo < 0 or hi >= n_experts:
+            raise ValueError(f"replayed expert id outside [0, {n_experts}): [{lo}, {hi}]")
     if not use_cuda_kernels(logits):
         ids, gates = route_reference(logits, top_k, replay_ids)
         return group_reference(ids, gates, n_experts)
