@@ -21,6 +21,26 @@ class OutOfPages(RuntimeError):
 
 
 class PagedKVCache:
+    @staticmethod
+    def bytes_per_page(num_layers: int, page_size: int, hkv: int, head_dim: int, top_k: int,
+                       elem_bytes: int = 2) -> int:
+        """Device bytes one page holds: K and V of every layer plus the routed-expert capture."""
+        return num_layers * page_size * (2 * hkv * head_dim * elem_bytes + top_k)
+
+    @staticmethod
+    def pages_for_memory_fraction(fraction: float, total_bytes: int, used_bytes: int,
+                                  page_bytes: int) -> int:
+        """Pages that fit when this process may use ``fraction`` of the device's memory and
+        ``used_bytes`` are taken already (weights, workspaces): the sglang
+        ``--mem-fraction-static`` rule, applied to the KV pool."""
+        if not 0.0 < fraction <= 1.0:
+            raise ValueError(f"memory fraction must be in (0, 1], got {fraction}")
+        pages = int((fraction * total_bytes - used_bytes) // page_bytes)
+        if pages < 1:
+            raise ValueError(f"no room for the KV cache: {fraction:g} of {total_bytes / 2**30:.1f} "
+                             f"GiB is below the {used_bytes / 2**30:.1f} GiB already in use")
+        return pages
+
     def __init__(self, num_layers: int, num_pages: int, page_size: int, hkv: int, head_dim: int,
                  top_k: int, device, dtype=torch.bfloat16):
         self.num_layers, self.num_pages, self.page_size = num_layers, num_pages, page_size

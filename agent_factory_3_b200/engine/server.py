@@ -209,35 +209,102 @@ def build_app(engine: Engine, model_info: dict | None = None, faults=None) -> we
     return app
 
 
+# sglang launch flags that a reference launch script passes and that this engine accepts without
+# acting on them (one attention path, one scheduler loop, no mmap'd loader, metrics always on)
+_SGLANG_NO_EFFECT = ("--attention-backend", "--swa-full-tokens-ratio", "--scheduler-recv-interval",
+                     "--log-level", "--speculative-draft-model-quantization")
+_SGLANG_NO_EFFECT_SWITCHES = ("--trust-remote-code", "--weight-loader-disable-mmap",
+                              "--disable-cuda-graph-padding", "--enable-metrics",
+                              "--enable-cache-report", "--enable-return-routed-experts")
+
+
+def build_arg_parser() -> argparse.ArgumentParser:
+    """Engine flags, plus the sglang flags of the reference's launch scripts
+    (examples/wordle/serve.sh:55-86): ``--model-path``, ``--tp-size``, ``--dtype``,
+    ``--kv-cache-dtype``, ``--mem-fraction-static``, ``--speculative-algorithm DFLASH`` with
+    ``--speculative-dflash-block-size`` and ``--speculative-draft-model-path``, and switches that
+    need no action here (routed experts are returned whenever a request asks for them)."""
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", "--model-path", dest="model", default="gpt-oss-120b",
+                    help="preset name or checkpoint directory")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=30000)
+    ap.add_argument("--num-pages", type=int, default=None,
+                    help="KV pages (default 8192, or sized by --mem-fraction-static)")
+    ap.add_argument("--mem-fraction-static", type=float, default=None,
+                    help="size the KV pool so this process uses this fraction of device memory")
+    ap.add_argument("--page-size", type=int, default=64)
+    ap.add_argument("--max-running-requests", type=int, default=128)
+    ap.add_argument("--max-prefill-tokens", type=int, default=16384)
+    ap.add_argument("--lora-r", "--max-lora-rank", dest="lora_r", type=int, default=0,
+                    help="LoRA capacity (0 = no LoRA serving)")
+    ap.add_argument("--lora-targets", "--lora-target-modules", dest="lora_targets",
+                    default="q_proj,k_proj,v_proj,o_proj")
+    ap.add_argument("--seed", "--random-seed", dest="seed", type=int, default=0)
+    ap.add_argument("--tp-size", "--tp", dest="tp_size", type=int, default=None,
+                    help="tensor-parallel ranks; must match the torchrun world (one process per GPU)")
+    ap.add_argument("--dtype", default="bfloat16", choices=["auto", "bfloat16", "bf16"])
+    ap.add_argument("--kv-cache-dtype", default="auto",
+                    choices=["auto", "bfloat16", "bf16", "fp8_e4m3", "fp8_e5m2"],
+                    help="the KV cache is bf16; fp8 requests are accepted and noted")
+    ap.add_argument("--speculative-algorithm", type=str.lower, default="none",
+                    choices=["none", "block", "ngram", "dflash"],
+                    help="block (alias dflash): one-forward block draft model sharing the "
+                         "target's embeddings")
+    ap.add_argument("--speculative-num-draft-tokens", "--speculative-dflash-block-size",
+                    dest="speculative_num_draft_tokens", type=int, default=8)
+    ap.add_argument("--speculative-draft-layers", type=int, default=1)
+    ap.add_argument("--speculative-draft-model-path", default=None,
+                    help="accepted; the block draft is built from the target (its own layers "
+                         "random-initialised from --seed)")
+    ap.add_argument("--cuda-graphs", action="store_true", help="replay decode steps from CUDA graphs (TP=1)")
+    for f in _SGLANG_NO_EFFECT:
+        ap.add_argument(f, default=None, help=argparse.SUPPRESS)
+    for f in _SGLANG_NO_EFFECT_SWITCHES:
+        ap.add_argument(f, action="store_true", help=argparse.SUPPRESS)
+    return ap
+
+
+def resolve_args(a: argparse.Namespace, world: int) -> list[str]:
+    """Checks and maps the compatibility flags in place; returns notes for the log."""
+    notes = []
+    if a.tp_size is not None and a.tp_size != world:
+        raise SystemExit(f"--tp-size {a.tp_size} but {world} process(es): launch one process per "
+                         f"GPU, e.g. torchrun --nproc-per-node {a.tp_size} -m "
+                         "agent_factory_3_b200.engine.server ...")
+    if a.speculative_algorithm == "dflash":
+        a.speculative_algorithm = "block"
+        notes.append(f"DFLASH -> block draft of {a.speculative_num_draft_tokens} tokens")
+    if a.kv_cache_dtype.startswith("fp8"):
+        notes.append(f"--kv-cache-dtype {a.kv_cache_dtype}: the KV cache stays bf16")
+    if a.speculative_draft_model_path:
+        notes.append("--speculative-draft-model-path: the block draft is built from the target")
+    if a.num_pages is not None and a.mem_fraction_static is not None:
+        raise SystemExit("give --num-pages or --mem-fraction-static, not both")
+    ignored = [f for f in _SGLANG_NO_EFFECT if getattr(a, f[2:].replace("-", "_")) is not None]
+    ignored += [f for f in _SGLANG_NO_EFFECT_SWITCHES if getattr(a, f[2:].replace("-", "_"))]
+    if ignored:
+        notes.append("accepted with no effect: " + " ".join(ignored))
+    return notes
+
+
 def main():
     import torch
 
     from ..models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
     from ..models.gpt_oss.checkpoint import load_checkpoint
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--model", default="gpt-oss-120b", help="preset name or checkpoint directory")
-    ap.add_argument("--host", default="127.0.0.1")
-    ap.add_argument("--port", type=int, default=30000)
-    ap.add_argument("--num-pages", type=int, default=8192)
-    ap.add_argument("--page-size", type=int, default=64)
-    ap.add_argument("--max-running-requests", type=int, default=128)
-    ap.add_argument("--max-prefill-tokens", type=int, default=16384)
-    ap.add_argument("--lora-r", type=int, default=0, help="LoRA capacity (0 = no LoRA serving)")
-    ap.add_argument("--lora-targets", default="q_proj,k_proj,v_proj,o_proj")
-    ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--speculative-algorithm", choices=["none", "block", "ngram"], default="none",
-                    help="block: one-forward block draft model sharing the target's embeddings")
-    ap.add_argument("--speculative-num-draft-tokens", type=int, default=8)
-    ap.add_argument("--speculative-draft-layers", type=int, default=1)
-    ap.add_argument("--cuda-graphs", action="store_true", help="replay decode steps from CUDA graphs (TP=1)")
+    ap = build_arg_parser()
     a = ap.parse_args()
     from pathlib import Path
-    p = Path(a.model)
-    cfg = GptOssConfig.load(p / "config.json") if (p / "config.json").exists() else GptOssConfig.preset(a.model)
-    lora = LoraConfig(r=a.lora_r, lora_alpha=2 * a.lora_r, target_modules=a.lora_targets.split(",")) if a.lora_r else None
     import os
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    for note in resolve_args(a, world):
+        if rank == 0:
+            print(f"[engine] {note}", flush=True)
+    p = Path(a.model)
+    cfg = GptOssConfig.load(p / "config.json") if (p / "config.json").exists() else GptOssConfig.preset(a.model)
+    lora = LoraConfig(r=a.lora_r, lora_alpha=2 * a.lora_r, target_modules=a.lora_targets.split(",")) if a.lora_r else None
     if world > 1:   # tensor parallel under torchrun: rank 0 serves HTTP, the others follow
         import datetime
         import torch.distributed as dist
@@ -267,7 +334,19 @@ def main():
     elif a.speculative_algorithm == "ngram":
         from .spec import NgramDrafter
         drafter = NgramDrafter(block=a.speculative_num_draft_tokens)
-    eng = Engine(model, num_pages=a.num_pages, page_size=a.page_size,
+    num_pages = a.num_pages if a.num_pages is not None else 8192
+    if a.mem_fraction_static is not None:
+        from .kv_cache import PagedKVCache
+        free, total = torch.cuda.mem_get_info(dev)
+        page_bytes = PagedKVCache.bytes_per_page(cfg.num_hidden_layers, a.page_size,
+                                                 cfg.num_key_value_heads // world, cfg.head_dim,
+                                                 cfg.num_experts_per_tok)
+        num_pages = PagedKVCache.pages_for_memory_fraction(a.mem_fraction_static, total,
+                                                           total - free, page_bytes)
+        if rank == 0:
+            print(f"[engine] --mem-fraction-static {a.mem_fraction_static:g}: {num_pages} KV pages "
+                  f"of {a.page_size} tokens", flush=True)
+    eng = Engine(model, num_pages=num_pages, page_size=a.page_size,
                  max_running=a.max_running_requests, max_prefill_tokens=a.max_prefill_tokens,
                  tp=tp, tp_shards=shards, drafter=drafter,
                  cuda_graphs=a.cuda_graphs and world == 1)

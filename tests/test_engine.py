@@ -285,3 +285,42 @@ def test_engine_batches_requests_of_different_adapters_together():
     assert all(len(o["output_ids"]) == 6 for o in outs)
     assert calls["mixed"] > 0
     assert bad["meta_info"]["finish_reason"]["type"] == "abort"
+
+
+def test_server_accepts_the_reference_launch_flags():
+    """The sglang flag set of a reference launch script parses, maps onto this engine's options
+    and leaves a note for each flag that has no effect here."""
+    from agent_factory_3_b200.engine.server import build_arg_parser, resolve_args
+    argv = ["--model-path", "/models/gpt-oss-120b", "--tp-size", "2", "--dtype", "bfloat16",
+            "--attention-backend", "fa3", "--kv-cache-dtype", "fp8_e4m3",
+            "--mem-fraction-static", "0.82", "--max-running-requests", "128",
+            "--swa-full-tokens-ratio", "0.1", "--trust-remote-code", "--host", "0.0.0.0",
+            "--port", "30000", "--scheduler-recv-interval", "16", "--log-level", "info",
+            "--enable-return-routed-experts", "--weight-loader-disable-mmap",
+            "--disable-cuda-graph-padding", "--enable-metrics", "--enable-cache-report",
+            "--speculative-algorithm", "DFLASH", "--speculative-draft-model-path", "/models/d",
+            "--speculative-draft-model-quantization", "fp8", "--speculative-dflash-block-size", "10"]
+    a = build_arg_parser().parse_args(argv)
+    notes = resolve_args(a, world=2)
+    assert a.model == "/models/gpt-oss-120b" and a.tp_size == 2 and a.port == 30000
+    assert a.speculative_algorithm == "block" and a.speculative_num_draft_tokens == 10
+    assert a.mem_fraction_static == 0.82 and a.num_pages is None
+    text = " ".join(notes)
+    assert "stays bf16" in text and "--attention-backend" in text and "--enable-metrics" in text
+    with pytest.raises(SystemExit):          # two ranks asked for, one process launched
+        resolve_args(build_arg_parser().parse_args(["--tp-size", "2"]), world=1)
+    with pytest.raises(SystemExit):
+        resolve_args(build_arg_parser().parse_args(["--num-pages", "8", "--mem-fraction-static",
+                                                    "0.5"]), world=1)
+
+
+def test_kv_pages_for_memory_fraction():
+    cfg = GptOssConfig.preset("gpt-oss-120b")
+    page = PagedKVCache.bytes_per_page(cfg.num_hidden_layers, 64, cfg.num_key_value_heads,
+                                       cfg.head_dim, cfg.num_experts_per_tok)
+    assert page == 36 * 64 * (2 * 8 * 64 * 2 + 4)
+    gib = 1 << 30
+    n = PagedKVCache.pages_for_memory_fraction(0.82, 180 * gib, 70 * gib, page)
+    assert n == int((0.82 * 180 * gib - 70 * gib) // page) and n > 0
+    with pytest.raises(ValueError):
+        PagedKVCache.pages_for_memory_fraction(0.3, 180 * gib, 70 * gib, page)
