@@ -178,3 +178,36 @@ def test_lora_grads_match_autograd():
         ref = params[n].grad
         err = (g - ref).abs().max().item()
         assert err <= 1e-2 * (ref.abs().max().item() + 1e-6), (n, err, ref.abs().max().item())
+
+
+def test_reference_style_entry_points(tmp_path):
+    """The reference's gpt_oss entry points: the dequant config sets the expert compute type,
+    routing replay needs no patch, and from_pretrained reloads a saved checkpoint exactly."""
+    from agent_factory_3_b200.models.gpt_oss import (Mxfp4Bf16DequantConfig,
+                                                     enable_routing_replay, from_pretrained)
+    from agent_factory_3_b200.models.gpt_oss.checkpoint import save_checkpoint
+    m = _model()
+    m.cfg.save(tmp_path / "config.json")
+    save_checkpoint(m, tmp_path)
+    cfg = Mxfp4Bf16DequantConfig(dequant_dtype="fp8")
+    assert cfg.to_dict()["dequant_dtype"] == "fp8"
+    m2 = enable_routing_replay(from_pretrained(tmp_path, quantization_config=cfg.to_dict()))
+    assert all(layer.mlp.dequant_dtype == "fp8" for layer in m2.layers)
+    assert m2.embed_tokens.dtype == torch.bfloat16
+    m2 = from_pretrained(tmp_path, dtype=torch.float32)   # bf16 expert compute by default
+    assert m2 is enable_routing_replay(m2)
+    ids, pos, cu = _packed([21, 9], m.cfg.vocab_size, seed=5)
+    m2.gradient_checkpointing = False
+    # the checkpoint holds bf16 dense weights, so compare with the same files loaded the usual way
+    from agent_factory_3_b200.models.gpt_oss.checkpoint import load_checkpoint
+    m3 = GptOssForCausalLM(m.cfg, dtype=torch.float32)
+    assert not load_checkpoint(tmp_path, m3)
+    m3.gradient_checkpointing = False
+    with torch.no_grad():
+        h1, rec = m3.forward_hidden(ids, pos, cu, record_routing=True)
+        h2 = m2.forward_hidden(ids, pos, cu, routing_indices=rec)
+    torch.testing.assert_close(h2, h1)
+    with pytest.raises(ValueError):
+        Mxfp4Bf16DequantConfig(dequant_dtype="e5m2")
+    with pytest.raises(TypeError):
+        enable_routing_replay(torch.nn.Linear(2, 2))
