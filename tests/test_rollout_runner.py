@@ -154,3 +154,17 @@ def test_harmony_roundtrip():
     out = ENC.parse_messages_from_completion_tokens(comp)
     assert [(m.channel, m.recipient, m.content, m.content_type) for m in out] == \
         [("analysis", None, "hi", None), ("commentary", "functions.f", '{"a":1}', "json")]
+
+
+def test_rollout_package_exports_the_reference_names():
+    import agent_factory_3_b200.rollout as R
+    names = {"ConversationConfig", "ExtraRoundConfig", "LoopConfig", "RecordConfig", "SamplingParams",
+             "SegmentTemperatureConfig", "EndReason", "StepType", "TruncationReason", "TokenBudget",
+             "SegmentMeta", "BaseStep", "InitStep", "AssistantStep", "ToolStep", "Step",
+             "ReactResult", "McpExecutor", "ToolCallReport", "ToolErrorType", "ConversationBuilder",
+             "UnifiedReactRunner", "CompletionResult", "RolloutConfig", "RolloutResult",
+             "execute_rollout"}
+    assert names <= set(R.__all__)
+    assert all(getattr(R, n) is not None for n in names)
+    from agent_factory_3_b200.rollout.runner import UnifiedReactRunner
+    assert R.UnifiedReactRunner is UnifiedReactRunner
