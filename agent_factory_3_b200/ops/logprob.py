@@ -111,6 +111,13 @@ class _LogprobRef(torch.autograd.Function):
         return dh.to(hidden.dtype), None, None, None, None
 
 
+def linear_logprob_entropy_torch(hidden: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor,
+                                 temperature: float = 1.0, chunk: int = 512):
+    """The chunked PyTorch path of ``linear_logprob_entropy`` on any device (exact log-softmax
+    per chunk of rows, manual backward), for cross-checking the fused kernel."""
+    return _LogprobRef.apply(hidden, weight, labels, float(temperature), int(chunk))
+
+
 def linear_logprob_entropy(hidden: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor,
                            temperature: float = 1.0, chunk: int = 16384):
     """(logprob [T] fp32, entropy [T] fp32) of ``labels`` under softmax(hidden W^T / temp)."""
