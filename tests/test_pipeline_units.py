@@ -182,3 +182,39 @@ def test_worker_lanes_bound_concurrency_and_report_failures(monkeypatch):
     assert sorted((g, i) for g, i, _ in got) == sorted((f"g{i // 2}", i % 2) for i in range(8))
     failed = [r for _, _, r in got if not r.success]
     assert len(failed) == 1 and failed[0].rollout_id == "t3" and "boom" in failed[0].error
+
+
+def test_server_pool_least_busy_and_release():
+    import asyncio
+    from agent_factory_3_b200.rollout.parallel.server_pool import ServerPool
+
+    async def run():
+        pool = ServerPool(["http://a", "http://b", "http://c"])
+        got = [await pool.acquire() for _ in range(4)]
+        assert got == ["http://a", "http://b", "http://c", "http://a"]   # ties go to list order
+        await pool.release("http://b")
+        await pool.release("http://b")          # never below zero
+        assert await pool.acquire() == "http://b"
+        assert pool.stats() == {"http://a": 2, "http://b": 1, "http://c": 1}
+    asyncio.run(run())
+    with pytest.raises(ValueError):
+        ServerPool([])
+
+
+def test_rollout_stats_and_monitor():
+    from agent_factory_3_b200.rollout.parallel.execution_monitor import ExecutionMonitor
+    from agent_factory_3_b200.rollout.parallel.postprocessing import (compute_stats_batch,
+                                                                       validate_routing_indices)
+    ok, bad = _result("a"), _result("b")
+    bad.result.routing_indices[0] = np.full((2, 2), 200, np.uint8)   # expert id past 128
+    out = compute_stats_batch([ok, bad], num_experts=128)
+    assert out[0].routing_valid and not out[1].routing_valid
+    assert out[0].completion_tokens_count == 3 and out[0].num_rounds == 1
+    assert validate_routing_indices(ok.result, num_experts=2)
+    assert not validate_routing_indices(ok.result, num_experts=1)
+    mon = ExecutionMonitor(total=2, use_tqdm=False)
+    for r in out:
+        mon.update(r)
+    s = mon.summary()
+    assert s["done"] == 2 and s["generated_tokens"] == 6 and s["end_reasons"] == {"completed": 2}
+    mon.close()
