@@ -168,3 +168,42 @@ def test_rollout_package_exports_the_reference_names():
     assert all(getattr(R, n) is not None for n in names)
     from agent_factory_3_b200.rollout.runner import UnifiedReactRunner
     assert R.UnifiedReactRunner is UnifiedReactRunner
+
+
+def test_vllm_backend_against_a_fake_openai_server():
+    """Token ids in, token ids and log-probs out through /v1/completions (the client that the
+    reference keeps for OpenAI-style servers)."""
+    from aiohttp import web
+    from aiohttp.test_utils import TestServer
+
+    from agent_factory_3_b200.rollout.config import RecordConfig, SamplingParams
+    from agent_factory_3_b200.rollout.llm_backend.vllm_backend import VLLMBackend
+    seen = {}
+
+    async def completions(request):
+        body = await request.json()
+        seen.update(body)
+        return web.json_response({
+            "choices": [{"finish_reason": "stop",
+                         "logprobs": {"tokens": ["token_id:7", "token_id:9"],
+                                      "token_logprobs": [-0.25, -1.5]}}],
+            "usage": {"prompt_tokens": 3, "completion_tokens": 2}})
+
+    async def run():
+        app = web.Application()
+        app.router.add_post("/v1/completions", completions)
+        srv = TestServer(app)
+        await srv.start_server()
+        try:
+            be = VLLMBackend(str(srv.make_url("")), "gpt-oss")
+            r = await be.generate([1, 2, 3], 16, [200002], SamplingParams(temperature=0.5, top_k=20,
+                                                                          seed=4),
+                                  record=RecordConfig(logprobs=True))
+            await be.close()
+            return r
+        finally:
+            await srv.close()
+    r = asyncio.run(run())
+    assert r.token_ids == [7, 9] and r.logprobs == [-0.25, -1.5] and r.finish_reason == "stop"
+    assert seen["prompt"] == [1, 2, 3] and seen["top_k"] == 20 and seen["seed"] == 4
+    assert seen["stop_token_ids"] == [200002] and seen["logprobs"] == 1
