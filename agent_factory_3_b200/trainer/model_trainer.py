@@ -16,7 +16,8 @@ What differs (B200 design):
     sharded) instead of per-parameter collectives;
   * loss/metric reductions are packed into one all-reduce;
   * rank 0 plans the step's packing and scatters to each rank only the samples of that rank's
-    buckets; no rank receives the whole step.
+    buckets, with their arrays sent as raw bytes (parallel/payload.py); no rank receives the
+    whole step.
 """
 from __future__ import annotations
 
@@ -32,6 +33,7 @@ import torch.distributed as dist
 
 from ..models.gpt_oss import GptOssConfig, GptOssForCausalLM, LoraConfig
 from ..models.gpt_oss import checkpoint as ckpt
+from ..parallel import payload
 from ..parallel.rpc import RPCMixin, rpc_method
 from .data.collator import DataCollatorWithPacking, shift_completion_mask
 from .data.sampler import DeterministicPackedBatchSampler
@@ -317,10 +319,8 @@ class ModelTrainer(RPCMixin):
         """Every rank: receive this rank's (samples, microbatch index lists) from rank 0,
         then forward/backward each microbatch and take the optimizer step."""
         if self._rpc_active():
-            box = [None]
-            dist.scatter_object_list(box, self._outbox if self.rank == 0 else None, src=0,
-                                     group=self._rpc_group)
-            samples, plan = box[0]
+            samples, plan = payload.scatter(self._outbox if self.rank == 0 else None,
+                                            group=self._rpc_group, src=0)
         else:
             samples, plan = self._outbox[0]
         self.model.train()
