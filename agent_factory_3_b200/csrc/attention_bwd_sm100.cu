@@ -14,9 +14,10 @@
 //   dQ   = dS K         (A = dS^T read as MN-major from shared memory, B = K as MN-major)
 //                                                                      TMEM cols 384..447
 // K and V are the A operands of S^T / dP^T and sit in TMEM too (cols 448..479, 480..511,
-// copied there once per CTA).  With N = 64 an MMA that reads both operands from shared memory
-// is bound by shared-memory bandwidth, the busiest unit of this kernel, so every product except
-// dQ takes its A operand from TMEM and reads only the 2 KB B slice per instruction.
+// copied there once per CTA).  With N = 64, an MMA that reads both operands from shared memory
+// needs 6 KB per 32 tensor cycles, more than the 128 B per cycle that shared memory delivers.
+// So every product except dQ takes its A operand from TMEM and reads only its 2 KB B slice
+// from shared memory.
 // The eight softmax warps work on one half at a time (warp quarter = 32 key rows, warps 4-7
 // the first 32 queries of the half, warps 12-15 the other 32); while they compute one half,
 // the tensor core runs dV / dK of the other half and the next block's S^T / dP^T of it.
