@@ -73,9 +73,15 @@ class TrainingConfig(BaseModel):
     max_capacity: int = 20000
     pad_to_multiple_of_training: int = 1024
     # rank balancing of the packing plan: "tokens" (the reference's rule) or "cost" (tokens
-    # plus the quadratic attention work, n + n^2 / packing_attention_tokens per sample)
+    # plus the quadratic attention work, n + n^2 / packing_attention_tokens per sample).  The
+    # default is the sequence length at which a sample's attention time equals the rest of its
+    # step time. It comes from a gpt-oss-120b step on one B200 (131072 tokens in two samples of
+    # 112105 and 18967):
+    #   - attention forward + backward: 11.2 s, over sum(n^2) = 1.29e10;
+    #   - everything else: 4.7 s, over 131072 tokens;
+    #   - (4.7 / 131072) / (11.2 / 1.29e10) = about 41k tokens.
     packing_balance: Literal["tokens", "cost"] = "cost"
-    packing_attention_tokens: int = 32768
+    packing_attention_tokens: int = 40960
     dataloader_num_workers: int = 0
     # routing replay
     use_routing_replay: bool = True
